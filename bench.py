@@ -1,0 +1,518 @@
+#!/usr/bin/env python
+"""MSDA forward + backward benchmark on B200 (BEVFormer-base spatial cross-attention).
+
+One *step* is the reference benchmark's ``forward-backward`` scope
+(``benchmarks/msda/benchmark_msda.py:85-119`` in the muSPACE tree): the forward
+launch, the zero fill of the fp32 ``grad_value`` accumulator and the backward
+launch, through the C-ABI (``ms_deform_attn_forward`` / ``ms_deform_attn_backward``)
+on device-resident inputs. The workload is BASELINE config 4: the c2 shapes
+(6 cameras x 4 levels [(116,200),(58,100),(29,50),(15,25)], Lq=10000, 8 heads x
+32 channels, 8 points) at batch 8 x 6 cameras = 48 images, bf16 storage with fp32
+accumulation, 10% of the locations out of bounds. Inputs are seeded synthetic
+tensors (no dataset) and total 1.7 GB, far beyond the 126 MB L2, so no flush is
+needed between steps.
+
+``value`` is effective GB/s: the algorithmic (compulsory) bytes of the step
+(fwd: value + locations + weights + output; bwd: the same reads plus fp32
+writes of the three gradients) over the device time, summed over ranks. Each
+rank processes its own 48-image shard (weak scaling, no collective on the data
+path); ``--scaling strong`` splits the 48 images across ranks instead.
+``--variant query`` runs the bs=1 form: one 6-camera sample, queries split
+across ranks, value replicated, fp32 ``grad_value`` reduce-scattered with NCCL.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from muspace_b200 import cases  # noqa: E402
+
+METRIC = "MSDA fwd+bwd µs & effective HBM GB/s (BEVFormer-base SCA), 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 2**20
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--config", default="c4", choices=sorted(cases.CONFIGS))
+    p.add_argument("--dtype", choices=("bfloat16", "float32"), default=None)
+    p.add_argument("--scaling", choices=("weak", "strong"), default="weak")
+    p.add_argument("--variant", choices=("batch", "query"), default="batch")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--quiet", action="store_true", help="print only the JSON line")
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------------------
+# helpers
+# --------------------------------------------------------------------------------------
+
+
+def _dtype(args, cfg) -> torch.dtype:
+    name = args.dtype or cfg.dtypes[0]
+    return {"bfloat16": torch.bfloat16, "float32": torch.float32}[name]
+
+
+def _dtype_tag(dtype) -> str:
+    return {torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
+
+
+def _peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs: STREAM-style copy)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+def _traffic(kernel: str, workload: str, launch_units: float):
+    """DRAM bytes per launch from the committed ncu summary, scaled by units."""
+    path = ROOT / "profiles" / "dram_traffic.json"
+    try:
+        entry = json.loads(path.read_text())[kernel]
+    except Exception:
+        return None, None
+    per_unit = entry["dram_bytes"] / entry["units"]
+    return per_unit * launch_units, entry.get("source")
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region (5 Hz)."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL,
+                text=True,
+            )
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        if self.proc is None or not getattr(self, "out", ""):
+            return None
+        rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        power = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons,
+            "samples": len(rows),
+            "power_w_max": max(power) if power else None,
+        }
+
+
+# --------------------------------------------------------------------------------------
+# CPU legs (the oracle port of the reference's PyTorch path)
+# --------------------------------------------------------------------------------------
+
+
+def _cpu_sample_cfg(cfg):
+    """One camera image of the workload: about 1 s of fwd+bwd on 8 host threads."""
+    return cfg.with_(batch=1)
+
+
+def cpu_time_per_call(cfg, dtype, reps: int, warmup: int = 1):
+    from oracle.msda_torch import msda_grid_sample_fwd_bwd
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = _cpu_sample_cfg(cfg)
+    inp = cases.make_inputs(sample, dtype=dtype, seed=2333)
+    # the reference's PyTorch path runs in the storage dtype's fp32 form on CPU
+    args = [inp[k].float() if inp[k].dtype.is_floating_point else inp[k] for k in
+            ("value", "spatial_shapes", "sampling_locations", "attention_weights", "grad_output")]
+    for _ in range(warmup):
+        msda_grid_sample_fwd_bwd(*args)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        msda_grid_sample_fwd_bwd(*args)
+        times.append(time.perf_counter() - t0)
+    nbytes = cases.compulsory_bytes(sample, dtype)["total"]
+    return times, nbytes, sample, torch.get_num_threads()
+
+
+def cpu_baseline(cfg, dtype):
+    times, nbytes, sample, cores = cpu_time_per_call(cfg, dtype, reps=3)
+    t = statistics.median(times)
+    return {
+        "value": round(nbytes / t / 1e9, 4),
+        "unit": "GB/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": (
+            f"{sample.name} shapes at batch 1 (one camera image of the workload), fwd+bwd of the reference's "
+            f"PyTorch grid_sample formulation (oracle/msda_torch.py) on CPU tensors, median of 3 after 1 warm-up; "
+            f"{t * 1e3:.1f} ms per call, {nbytes / 1e6:.1f} MB compulsory"
+        ),
+        "ms_per_call": round(t * 1e3, 3),
+    }
+
+
+def run_reference(args, cfg, dtype, rank: int):
+    if rank != 0:
+        return
+    times, nbytes, sample, cores = cpu_time_per_call(cfg, dtype, reps=args.steps, warmup=args.warmup)
+    total = sum(times)
+    value = nbytes * len(times) / total / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total / len(times) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": args.scaling,
+        "vs_baseline": None,
+        "dtype": _dtype_tag(dtype),
+        "data": "synthetic",
+        "config": {"workload": _workload_name(cfg, dtype, args), "sample": f"{sample.name} at batch 1"},
+        "cpu_baseline": {
+            "value": round(value, 4),
+            "unit": "GB/s",
+            "cores": cores,
+            "kind": "port",
+            "sample": "one camera image per step (batch 1 of the workload), reference PyTorch grid_sample path "
+                      "restated in oracle/msda_torch.py, fwd+bwd on CPU tensors",
+        },
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _workload_name(cfg, dtype, args) -> str:
+    if args.variant == "query":
+        return f"config 4 bs=1 variant: {cfg.name} shapes at batch 6, queries split across ranks, grad_value reduce-scatter"
+    return (
+        f"config 4: BEVFormer-base SCA MSDA fwd+bwd, {cfg.batch} camera images per "
+        f"{'rank' if args.scaling == 'weak' else 'job'}, {_dtype_tag(dtype)} storage, fp32 accumulate"
+    )
+
+
+# --------------------------------------------------------------------------------------
+# GPU arm
+# --------------------------------------------------------------------------------------
+
+
+class Step:
+    """Device buffers and the two C-ABI calls of one forward-backward step."""
+
+    def __init__(self, inp: dict, dtype, device):
+        from muspace_b200.runtime.native import native_function
+
+        self.fwd = native_function("ms_deform_attn_forward")
+        self.bwd = native_function("ms_deform_attn_backward")
+        self.inp = inp
+        self.names = ("value", "spatial_shapes", "level_start_index", "sampling_locations", "attention_weights")
+        self.out = torch.empty(inp["grad_output"].shape, dtype=dtype, device=device)
+        self.gv = torch.zeros(inp["value"].shape, dtype=torch.float32, device=device)
+        self.gl = torch.empty(inp["sampling_locations"].shape, dtype=torch.float32, device=device)
+        self.gw = torch.empty(inp["attention_weights"].shape, dtype=torch.float32, device=device)
+
+    def __call__(self, events=None):
+        a = [self.inp[n] for n in self.names]
+        if events:
+            events[0].record()
+        self.fwd(*a, self.out, 64)
+        if events:
+            events[1].record()
+        self.gv.zero_()
+        if events:
+            events[2].record()
+        self.bwd(*a, self.inp["grad_output"], self.gv, self.gl, self.gw, 64)
+        if events:
+            events[3].record()
+
+
+def run_b200(args, cfg, dtype, rank, world, device):
+    import torch.distributed as dist
+
+    distributed = world > 1
+    if args.variant == "query":
+        return run_query_variant(args, cfg, dtype, rank, world, device)
+    if args.scaling == "strong":
+        if cfg.batch % world:
+            raise SystemExit(f"strong scaling needs batch {cfg.batch} divisible by {world}")
+        local = cfg.with_(batch=cfg.batch // world)
+    else:
+        local = cfg
+    inp = cases.make_inputs(local, dtype=dtype, seed=2333 + 7919 * rank, device=device)
+    step = Step(inp, dtype, device)
+    units = cases.compulsory_bytes(local, dtype)
+    fwd_bytes, bwd_bytes = units["fwd"], units["bwd"]
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # per-kernel durations: a separate pass with events between the launches
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for e in ev:
+        step(e)
+    torch.cuda.synchronize()
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    fill_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+
+    # the timed region: K steps bracketed by a barrier and a synchronize
+    if distributed:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device.index) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    if distributed:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+    if distributed:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    job_bytes = (fwd_bytes + bwd_bytes) * world
+    value = job_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
+
+    e2e = None if args.no_e2e else run_e2e(args, local, dtype, inp, device, world, distributed)
+
+    if rank != 0:
+        return None
+    peak, peak_src = _peaks()
+    dominant, dom_ms, dom_bytes = ("ms_deformable_backward", bwd_ms, bwd_bytes) if bwd_ms >= fwd_ms else (
+        "ms_deformable_forward", fwd_ms, fwd_bytes)
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    traffic, traffic_src = _traffic(dominant, local.name, local.batch)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "us_per_call": round(ms_per_step * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": args.scaling,
+        "vs_baseline": None,
+        "dtype": _dtype_tag(dtype),
+        "data": "synthetic",
+        "config": {
+            "workload": _workload_name(local, dtype, args),
+            "batch_per_rank": local.batch,
+            "global_batch": local.batch * world,
+            "queries": local.queries,
+            "levels": [list(s) for s in local.shapes],
+            "points": local.points,
+            "heads": local.heads,
+            "channels": local.channels,
+            "parallelism": f"batch-sharded x{world} (no collective)",
+            "l2": f"inputs {sum(t.numel() * t.element_size() for t in inp.values()) / 1e9:.2f} GB per rank > 126 MB L2; no flush",
+            "scope": "forward launch + grad_value zero fill + backward launch through the C-ABI (reference forward-backward scope)",
+            "compulsory_bytes_per_step_per_rank": fwd_bytes + bwd_bytes,
+        },
+        "kernels_ms": {"forward": round(fwd_ms, 4), "grad_value_fill": round(fill_ms, 4), "backward": round(bwd_ms, 4)},
+        "roofline": {
+            "bound": "hbm",
+            "kernel": dominant,
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "peak_source": peak_src,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": None if traffic is None else int(traffic),
+            "traffic_source": traffic_src,
+            "algorithmic_bytes": dom_bytes,
+        },
+        "gpu_launches": 2 * args.steps * world,
+        "gpu_launches_per_rank": 2 * args.steps,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, dtype)
+    return line
+
+
+def run_e2e(args, local, dtype, inp, device, world, distributed):
+    """The same step through the C-ABI with host buffers: pinned H2D of the
+    inputs and D2H of the output and the three gradients, every step."""
+    import torch.distributed as dist
+
+    host_in = {k: v.cpu().pin_memory() for k, v in inp.items() if k not in ("spatial_shapes", "level_start_index")}
+    dev_in = dict(inp)
+    step = Step(dev_in, dtype, device)
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (step.out, step.gv, step.gl, step.gw)]
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    steps = max(3, min(args.steps, 10))
+
+    def one():
+        for k, t in host_in.items():
+            dev_in[k].copy_(t, non_blocking=True)
+        step()
+        for dst, src in zip(host_out, (step.out, step.gv, step.gl, step.gw)):
+            dst.copy_(src, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    if distributed:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        one()
+    end.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if distributed:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    nbytes = cases.compulsory_bytes(local, dtype)["total"] * world
+    return {
+        "value": round(nbytes / (ms / 1e3) / 1e9, 3),
+        "unit": "GB/s",
+        "h2d_bytes_per_step": h2d,
+        "d2h_bytes_per_step": d2h,
+        "ms_per_step": round(ms, 3),
+        "steps": steps,
+        "path": "pinned host buffers -> cudaMemcpyAsync -> ms_deform_attn_forward/backward (C-ABI) -> pinned host",
+    }
+
+
+def run_query_variant(args, cfg, dtype, rank, world, device):
+    from muspace_b200.sharding import QueryShardedStep
+
+    sample = cases.CONFIGS["c2"].with_(locations=cfg.locations)
+    inp = cases.make_inputs(sample, dtype=dtype, seed=2333, device=device)
+    step = QueryShardedStep(inp, dtype, rank, world)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device.index) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    nbytes = cases.compulsory_bytes(sample, dtype)["total"]
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC,
+        "value": round(nbytes / (ms / 1e3) / 1e9, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "us_per_call": round(ms * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": _dtype_tag(dtype),
+        "data": "synthetic",
+        "config": {"workload": _workload_name(sample, dtype, args), "parallelism": f"query-sharded x{world} + NCCL reduce_scatter(grad_value)"},
+        "gpu_launches": 2 * args.steps * world,
+        "clocks": clocks.summary(),
+    }
+
+
+def main():
+    args = parse_args()
+    cfg = cases.CONFIGS[args.config]
+    dtype = _dtype(args, cfg)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, dtype, rank)
+        return
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs CUDA devices for the b200 arm")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    try:
+        line = run_b200(args, cfg, dtype, rank, world, device)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

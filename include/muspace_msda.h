@@ -1,0 +1,167 @@
+/*
+ * muspace_msda.h -- C ABI of the B200 multi-scale deformable attention (MSDA)
+ * library, libmuspace_ops.so.
+ *
+ * The library replaces the MSDA exports of muSPACE's TVM-FFI module
+ * (csrc/ms_deformable_attn/ms_deform_attn_musa.mu:627-628): the same two entry
+ * points, the same argument order, dtype rules and validation, but bound as
+ * plain C over DLPack DLTensor views instead of tvm::ffi::TensorView, plus an
+ * explicit CUDA stream and an int status instead of a thrown ICHECK.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensors live on the same CUDA device and are row-major contiguous.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and returns without synchronising. Calls on different streams
+ *     are independent; the library keeps no global state besides the
+ *     per-thread error message.
+ *   - Return 0 on success. On failure nothing is launched, a non-zero
+ *     msda_status_t is returned and msda_last_error() describes it.
+ *   - value, sampling_locations, attention_weights, output and grad_output
+ *     share one storage dtype, float32 or bfloat16; geometry, interpolation
+ *     and every sum are evaluated in fp32 whatever the storage dtype.
+ *     spatial_shapes and level_start_index are int64; the three gradient
+ *     buffers are always float32.
+ *   - Layouts: value (B, Lin, Hh, D); spatial_shapes (L, 2) as (H, W);
+ *     level_start_index (L); sampling_locations (B, Lq, Hh, L, P, 2) with the
+ *     last dim (x, y) in [0, 1]; attention_weights (B, Lq, Hh, L, P);
+ *     output / grad_output (B, Lq, Hh * D).
+ *   - Sampling follows torch.nn.functional.grid_sample(mode="bilinear",
+ *     padding_mode="zeros", align_corners=False): corners outside a level
+ *     read as zero and receive no gradient.
+ */
+#ifndef MUSPACE_MSDA_H_
+#define MUSPACE_MSDA_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MSDA_API __attribute__((visibility("default")))
+#else
+#define MSDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef DLPACK_DLPACK_H_
+/* ABI-compatible subset of DLPack (v0.6 .. v1.x). Include <dlpack/dlpack.h>
+ * before this header to use the full definitions instead. */
+typedef enum {
+  kDLCPU = 1,
+  kDLCUDA = 2,
+  kDLCUDAHost = 3,
+  kDLCUDAManaged = 13,
+} DLDeviceType;
+
+typedef struct {
+  DLDeviceType device_type;
+  int32_t device_id;
+} DLDevice;
+
+typedef enum {
+  kDLInt = 0U,
+  kDLUInt = 1U,
+  kDLFloat = 2U,
+  kDLBfloat = 4U,
+} DLDataTypeCode;
+
+typedef struct {
+  uint8_t code;
+  uint8_t bits;
+  uint16_t lanes;
+} DLDataType;
+
+typedef struct {
+  void *data;
+  DLDevice device;
+  int32_t ndim;
+  DLDataType dtype;
+  int64_t *shape;
+  int64_t *strides; /* NULL = compact row-major */
+  uint64_t byte_offset;
+} DLTensor;
+#endif /* DLPACK_DLPACK_H_ */
+
+typedef enum {
+  MSDA_STATUS_OK = 0,
+  MSDA_STATUS_INVALID_ARGUMENT = 1, /* dtype, device, layout or shape rejected */
+  MSDA_STATUS_CUDA_ERROR = 2,       /* the CUDA runtime refused a launch */
+} msda_status_t;
+
+typedef enum {
+  MSDA_DTYPE_FLOAT32 = 0,
+  MSDA_DTYPE_BFLOAT16 = 1,
+} msda_dtype_t;
+
+/* Problem sizes for the plain-pointer entry points. */
+typedef struct {
+  int64_t batch;        /* B   */
+  int64_t spatial_size; /* Lin = sum over levels of H * W */
+  int64_t heads;        /* Hh  */
+  int64_t channels;     /* D   */
+  int64_t levels;       /* L   */
+  int64_t queries;      /* Lq  */
+  int64_t points;       /* P   */
+} msda_dims_t;
+
+/*
+ * Forward: output = MSDA(value, spatial_shapes, level_start_index,
+ * sampling_locations, attention_weights).
+ *
+ * Replaces ms_deform_attn_forward, csrc/ms_deformable_attn/ms_deform_attn_musa.mu:507-560
+ * (same argument order; `stream` is new). As there, B is read from value,
+ * L from spatial_shapes, Lq from sampling_locations dim 1 and P from its dim
+ * 4, and im2col_step must satisfy step = min(B, im2col_step) > 0 with
+ * B % step == 0. The reference launched once per chunk of `step` batch
+ * entries; here the whole batch is one launch, which gives the same result.
+ */
+MSDA_API int ms_deform_attn_forward(const DLTensor *value, const DLTensor *spatial_shapes,
+                           const DLTensor *level_start_index, const DLTensor *sampling_locations,
+                           const DLTensor *attention_weights, DLTensor *output, int im2col_step,
+                           void *stream);
+
+/*
+ * Backward.
+ *
+ * Replaces ms_deform_attn_backward, csrc/ms_deformable_attn/ms_deform_attn_musa.mu:561-626
+ * (same argument order; `stream` is new). grad_value, grad_sampling_loc and
+ * grad_attn_weight must be float32. As in the reference, grad_value is
+ * ACCUMULATED into, so the caller zeroes it first; grad_sampling_loc and
+ * grad_attn_weight are overwritten for every sample.
+ */
+MSDA_API int ms_deform_attn_backward(const DLTensor *value, const DLTensor *spatial_shapes,
+                            const DLTensor *level_start_index, const DLTensor *sampling_locations,
+                            const DLTensor *attention_weights, const DLTensor *grad_output,
+                            DLTensor *grad_value, DLTensor *grad_sampling_loc, DLTensor *grad_attn_weight,
+                            int im2col_step, void *stream);
+
+/*
+ * Plain-pointer forms of the two calls above for callers without DLPack: raw
+ * device pointers plus the sizes in `dims`. They perform the size checks but
+ * cannot see devices or strides, so the pointers must be contiguous device
+ * memory of the documented shapes on the current device. Same semantics as
+ * ms_deform_attn_forward / ms_deform_attn_backward (the reference has no
+ * plain-pointer export; these are the pointer-level core both wrap).
+ */
+MSDA_API int msda_forward(msda_dtype_t dtype, const msda_dims_t *dims, const void *value, const int64_t *spatial_shapes,
+                 const int64_t *level_start_index, const void *sampling_locations,
+                 const void *attention_weights, void *output, void *stream);
+
+MSDA_API int msda_backward(msda_dtype_t dtype, const msda_dims_t *dims, const void *value, const int64_t *spatial_shapes,
+                  const int64_t *level_start_index, const void *sampling_locations,
+                  const void *attention_weights, const void *grad_output, float *grad_value,
+                  float *grad_sampling_loc, float *grad_attn_weight, void *stream);
+
+/* Message of the last failed call on this thread ("" after a success). The
+ * reference raised it as a TVM-FFI exception (csrc/ffi/tensor_utils.hpp:13-34). */
+MSDA_API const char *msda_last_error(void);
+
+/* Library version string, "<major>.<minor>.<patch>". */
+MSDA_API const char *msda_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MUSPACE_MSDA_H_ */

@@ -1,0 +1,30 @@
+"""Import-path alias: ``mu_space`` is the B200 build in ``muspace_b200``.
+
+Code written against the reference package (``from mu_space.ops import
+multi_scale_deformable_attn``, ``from mu_space.patcher import default_patcher``,
+``import mu_space.runtime.native``) runs unchanged: every ``mu_space.<sub>``
+module listed below is the very same module object as ``muspace_b200.<sub>``,
+so monkeypatching one patches the other.
+"""
+
+import importlib
+import sys
+
+import muspace_b200
+from muspace_b200 import *  # noqa: F401,F403
+from muspace_b200 import __all__, __version__  # noqa: F401
+
+_SUBMODULES = (
+    "ops",
+    "ops.multi_scale_deformable_attn",
+    "runtime",
+    "runtime.kernel_dispatch",
+    "runtime.native",
+    "patcher",
+    "patcher.runtime",
+)
+for _name in _SUBMODULES:
+    sys.modules[f"{__name__}.{_name}"] = importlib.import_module(f"muspace_b200.{_name}")
+ops = muspace_b200.ops
+runtime = muspace_b200.runtime
+patcher = importlib.import_module("muspace_b200.patcher")

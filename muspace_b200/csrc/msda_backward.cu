@@ -1,0 +1,221 @@
+// MSDA backward on sm_100a.
+//
+// For every sample (b, q, h, l, p) with attention weight a and incoming
+// gradient g[c] = grad_out[b, q, h, c]:
+//   grad_value[corner k, c] += w_k * a * g[c]                    (scatter)
+//   grad_w[s]               = sum_c g[c] * bilinear_c
+//   grad_loc[s]             = (W * a * sum_c g[c] * d bilinear_c / dx,
+//                              H * a * sum_c g[c] * d bilinear_c / dy)
+// grad_value is accumulated into a caller-zeroed fp32 buffer; grad_loc and
+// grad_w are written (every sample, zero when it has no in-bounds corner).
+//
+// Replaces muSPACE's MUSA backward kernels
+// (csrc/ms_deformable_attn/ms_deform_attn_musa_kernel.muh:93-166 and 625-733,
+// launched by ms_deform_attn_musa.mu:114-453), which issue 4 x 32 scalar fp32
+// atomics per sample from one warp per head-row and serialise location /
+// weight loads through lane 0.
+//
+// B200 design: the same G-lane group per head-row as the forward. Each lane
+// scatters its 16-byte channel slice of every in-bounds corner with
+// red.global.add.v4.f32 (one vector reduction per 4 channels, no return
+// value), so a bf16 D=32 corner costs 8 vector REDs instead of 32 scalar
+// atomics. The three per-sample dot products are reduced across the group with
+// xor shuffles and one lane stores them.
+#include "msda_device.cuh"
+
+namespace msda {
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int m = G / 2; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m, G);
+  return v;
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(256) backward_vec_kernel(Dims d, const T* __restrict__ value,
+                                                           const int64_t* __restrict__ shapes,
+                                                           const int64_t* __restrict__ starts,
+                                                           const T* __restrict__ loc, const T* __restrict__ weight,
+                                                           const T* __restrict__ grad_out,
+                                                           float* __restrict__ grad_value,
+                                                           float* __restrict__ grad_loc,
+                                                           float* __restrict__ grad_weight) {
+  using V = Vec16<T>;
+  constexpr int kVec = V::kLanes;
+  extern __shared__ Level levels[];
+  stage_levels(levels, shapes, starts, d);
+
+  const int sub = threadIdx.x % G;
+  const int groups_per_cta = blockDim.x / G;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int row_stride = d.heads * d.channels;
+  const int samples = d.levels * d.points;
+
+  // Every lane of a warp runs the same number of loop trips (whole warps map
+  // to whole groups and the trip count only depends on the warp's first
+  // item), so the full-mask shuffles below are always convergent.
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * groups_per_cta;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * groups_per_cta + threadIdx.x / G;
+       item - (threadIdx.x % 32) / G < items; item += stride) {
+    const bool live = item < items;
+    const int64_t it = live ? item : items - 1;
+    const int h = static_cast<int>(it % d.heads);
+    const int64_t b = it / (static_cast<int64_t>(d.queries) * d.heads);
+    const int64_t vrow0 = (b * d.spatial_size) * row_stride + h * d.channels + sub * kVec;
+    const T* vbase = value + vrow0;
+    float* gbase = grad_value + vrow0;
+    const T* lp = loc + it * samples * 2;
+    const T* wp = weight + it * samples;
+
+    float g[kVec];
+    V::unpack(ld_stream16(grad_out + it * d.channels + sub * kVec, evict_first_policy()), g);
+
+    for (int l = 0; l < d.levels; ++l) {
+      const Level lv = levels[l];
+#pragma unroll 2
+      for (int p = 0; p < d.points; ++p) {
+        const int s = l * d.points + p;
+        const float2 xy = load_loc(lp + 2 * s);
+        const float a = to_f32(wp[s]);
+        Corners c;
+        float part_w = 0.0f, part_x = 0.0f, part_y = 0.0f;
+        if (live && corners(lv, xy.x, xy.y, c)) {
+          uint4 raw[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            raw[k] = c.row[k] >= 0 ? ldg16(vbase + static_cast<int64_t>(c.row[k]) * row_stride)
+                                   : make_uint4(0, 0, 0, 0);
+          float v[4][kVec];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) V::unpack(raw[k], v[k]);
+#pragma unroll
+          for (int i = 0; i < kVec; ++i) {
+            const float bil = c.w[0] * v[0][i] + c.w[1] * v[1][i] + c.w[2] * v[2][i] + c.w[3] * v[3][i];
+            const float dx = c.hh * (v[1][i] - v[0][i]) + c.lh * (v[3][i] - v[2][i]);
+            const float dy = c.hw * (v[2][i] - v[0][i]) + c.lw * (v[3][i] - v[1][i]);
+            part_w = fmaf(g[i], bil, part_w);
+            part_x = fmaf(g[i], dx, part_x);
+            part_y = fmaf(g[i], dy, part_y);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (c.row[k] < 0) continue;
+            const float wa = c.w[k] * a;
+            float* dst = gbase + static_cast<int64_t>(c.row[k]) * row_stride;
+#pragma unroll
+            for (int i = 0; i < kVec; i += 4)
+              red_add_v4(dst + i, wa * g[i], wa * g[i + 1], wa * g[i + 2], wa * g[i + 3]);
+          }
+        }
+        part_w = group_sum<G>(part_w);
+        part_x = group_sum<G>(part_x);
+        part_y = group_sum<G>(part_y);
+        if (live && sub == 0) {
+          const int64_t so = it * samples + s;
+          grad_weight[so] = part_w;
+          *reinterpret_cast<float2*>(grad_loc + 2 * so) =
+              make_float2(static_cast<float>(lv.width) * part_x * a, static_cast<float>(lv.height) * part_y * a);
+        }
+      }
+    }
+  }
+}
+
+// Any D: one thread per head-row, channels in a loop (no cross-thread
+// reduction needed); grad_value through scalar fp32 atomics.
+template <typename T>
+__global__ void __launch_bounds__(256) backward_scalar_kernel(Dims d, const T* __restrict__ value,
+                                                              const int64_t* __restrict__ shapes,
+                                                              const int64_t* __restrict__ starts,
+                                                              const T* __restrict__ loc,
+                                                              const T* __restrict__ weight,
+                                                              const T* __restrict__ grad_out,
+                                                              float* __restrict__ grad_value,
+                                                              float* __restrict__ grad_loc,
+                                                              float* __restrict__ grad_weight) {
+  extern __shared__ Level levels[];
+  stage_levels(levels, shapes, starts, d);
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int row_stride = d.heads * d.channels;
+  const int samples = d.levels * d.points;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; item < items;
+       item += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int h = static_cast<int>(item % d.heads);
+    const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
+    const int64_t vrow0 = (b * d.spatial_size) * row_stride + h * d.channels;
+    const T* g = grad_out + item * d.channels;
+    for (int l = 0; l < d.levels; ++l) {
+      const Level lv = levels[l];
+      for (int p = 0; p < d.points; ++p) {
+        const int64_t so = item * samples + l * d.points + p;
+        const float x = to_f32(loc[2 * so]), y = to_f32(loc[2 * so + 1]);
+        const float a = to_f32(weight[so]);
+        Corners c;
+        float part_w = 0.0f, part_x = 0.0f, part_y = 0.0f;
+        if (corners(lv, x, y, c)) {
+          for (int ch = 0; ch < d.channels; ++ch) {
+            const float gc = to_f32(g[ch]);
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              v[k] = c.row[k] >= 0 ? to_f32(value[vrow0 + static_cast<int64_t>(c.row[k]) * row_stride + ch]) : 0.0f;
+            const float bil = c.w[0] * v[0] + c.w[1] * v[1] + c.w[2] * v[2] + c.w[3] * v[3];
+            part_w = fmaf(gc, bil, part_w);
+            part_x = fmaf(gc, c.hh * (v[1] - v[0]) + c.lh * (v[3] - v[2]), part_x);
+            part_y = fmaf(gc, c.hw * (v[2] - v[0]) + c.lw * (v[3] - v[1]), part_y);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (c.row[k] >= 0)
+                atomicAdd(grad_value + vrow0 + static_cast<int64_t>(c.row[k]) * row_stride + ch, c.w[k] * a * gc);
+          }
+        }
+        grad_weight[so] = part_w;
+        grad_loc[2 * so] = static_cast<float>(lv.width) * part_x * a;
+        grad_loc[2 * so + 1] = static_cast<float>(lv.height) * part_y * a;
+      }
+    }
+  }
+}
+
+template <typename T, int G>
+static cudaError_t launch_backward_vec(const Dims& d, const Args& a, cudaStream_t stream) {
+  constexpr int kThreads = 256;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int64_t groups_per_cta = kThreads / G;
+  const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
+  const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
+  backward_vec_kernel<T, G><<<grid, kThreads, level_smem(d), stream>>>(
+      d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
+      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t stream) {
+  switch (vec_group(d.channels, sizeof(T), a)) {
+    case 1: return launch_backward_vec<T, 1>(d, a, stream);
+    case 2: return launch_backward_vec<T, 2>(d, a, stream);
+    case 4: return launch_backward_vec<T, 4>(d, a, stream);
+    case 8: return launch_backward_vec<T, 8>(d, a, stream);
+    case 16: return launch_backward_vec<T, 16>(d, a, stream);
+    case 32: return launch_backward_vec<T, 32>(d, a, stream);
+    default: break;
+  }
+  constexpr int kThreads = 256;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int64_t blocks = (items + kThreads - 1) / kThreads;
+  const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
+  backward_scalar_kernel<T><<<grid, kThreads, level_smem(d), stream>>>(
+      d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
+      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
+  if (d.batch == 0 || d.queries == 0 || d.heads == 0) return cudaSuccess;
+  return dtype == DType::kBF16 ? launch_backward_t<__nv_bfloat16>(d, a, stream)
+                               : launch_backward_t<float>(d, a, stream);
+}
+
+}  // namespace msda

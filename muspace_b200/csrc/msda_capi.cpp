@@ -1,0 +1,297 @@
+// extern "C" boundary of libmuspace_ops.so (declared in include/muspace_msda.h).
+//
+// Takes the place of the TVM-FFI binding of muSPACE's MSDA
+// (csrc/ms_deformable_attn/ms_deform_attn_musa.mu:507-628 and the checks of
+// csrc/ffi/tensor_utils.hpp:13-34): it validates DLPack views with the same
+// dtype / contiguity / im2col_step rules, adds the cross-tensor device check
+// the reference left out, and turns every failure into a status code plus a
+// per-thread message instead of an exception.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <string>
+
+#include "../../include/muspace_msda.h"
+#include "msda_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Failure {
+  int status;
+};
+
+[[noreturn]] void fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  throw Failure{status};
+}
+
+void require(bool ok, const std::string& msg) {
+  if (!ok) fail(MSDA_STATUS_INVALID_ARGUMENT, msg);
+}
+
+std::string dtype_name(DLDataType t) {
+  if (t.code == kDLFloat && t.bits == 32) return "float32";
+  if (t.code == kDLBfloat && t.bits == 16) return "bfloat16";
+  if (t.code == kDLFloat && t.bits == 16) return "float16";
+  if (t.code == kDLFloat && t.bits == 64) return "float64";
+  if (t.code == kDLInt && t.bits == 64) return "int64";
+  if (t.code == kDLInt && t.bits == 32) return "int32";
+  char buf[48];
+  std::snprintf(buf, sizeof(buf), "dtype(code=%u,bits=%u)", t.code, t.bits);
+  return buf;
+}
+
+bool same_dtype(DLDataType t, uint8_t code, uint8_t bits) { return t.code == code && t.bits == bits && t.lanes == 1; }
+
+// Device, dtype, rank and row-major contiguity of one view (size-1 dims may
+// carry any stride, as in DLPack's compactness rule).
+void check_tensor(const DLTensor* t, const char* name, uint8_t code, uint8_t bits, int ndim, int device_id) {
+  require(t != nullptr, std::string(name) + " is null");
+  require(t->device.device_type == kDLCUDA,
+          std::string(name) + " must be a CUDA tensor (DLPack device type kDLCUDA)");
+  require(t->device.device_id == device_id, std::string(name) + " is on CUDA device " +
+                                                std::to_string(t->device.device_id) + ", value is on device " +
+                                                std::to_string(device_id));
+  require(same_dtype(t->dtype, code, bits), std::string(name) + " must be " +
+                                                dtype_name(DLDataType{code, bits, 1}) + ", got " +
+                                                dtype_name(t->dtype));
+  require(t->ndim == ndim, std::string(name) + " must have " + std::to_string(ndim) + " dims, got " +
+                               std::to_string(t->ndim));
+  for (int i = 0; i < ndim; ++i) require(t->shape[i] >= 0, std::string(name) + " has a negative extent");
+  if (t->strides != nullptr) {
+    int64_t expect = 1;
+    for (int i = ndim - 1; i >= 0; --i) {
+      if (t->shape[i] != 1)
+        require(t->strides[i] == expect, std::string(name) + " must be contiguous");
+      expect *= t->shape[i];
+    }
+  }
+}
+
+void* data_of(const DLTensor* t) { return static_cast<char*>(t->data) + t->byte_offset; }
+
+void check_dims(const msda_dims_t& d) {
+  const int64_t kMax = std::numeric_limits<int32_t>::max();
+  require(d.batch >= 0 && d.spatial_size >= 0 && d.heads >= 0 && d.channels >= 0 && d.levels >= 0 &&
+              d.queries >= 0 && d.points >= 0,
+          "sizes must be non-negative");
+  require(d.batch <= kMax && d.spatial_size <= kMax && d.queries <= kMax && d.levels <= 4096 && d.points <= 4096,
+          "a size exceeds the supported range (B, Lin, Lq < 2^31; L, P <= 4096)");
+  require(d.heads * d.channels <= kMax && d.levels * d.points <= kMax, "Hh * D or L * P exceeds 2^31");
+}
+
+msda::Dims to_kernel_dims(const msda_dims_t& d) {
+  return msda::Dims{static_cast<int>(d.batch),   static_cast<int>(d.spatial_size), static_cast<int>(d.heads),
+                    static_cast<int>(d.channels), static_cast<int>(d.levels),       static_cast<int>(d.queries),
+                    static_cast<int>(d.points)};
+}
+
+void check_launch(cudaError_t err, const char* what) {
+  if (err != cudaSuccess)
+    fail(MSDA_STATUS_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorName(err) + ": " + cudaGetErrorString(err));
+}
+
+// Makes `device` current for the launch and restores the caller's device.
+struct DeviceGuard {
+  int previous = -1;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
+    if (previous != device) check_launch(cudaSetDevice(device), "cudaSetDevice");
+  }
+  ~DeviceGuard() {
+    int now = -1;
+    if (previous >= 0 && cudaGetDevice(&now) == cudaSuccess && now != previous) cudaSetDevice(previous);
+  }
+};
+
+// Shape checks shared by both directions; fills dims from the views the way
+// the reference does (ms_deform_attn_musa.mu:521-522).
+msda_dims_t dims_from_views(const DLTensor* value, const DLTensor* spatial, const DLTensor* start,
+                            const DLTensor* loc, const DLTensor* weight, int im2col_step) {
+  msda_dims_t d{};
+  d.batch = value->shape[0];
+  d.spatial_size = value->shape[1];
+  d.heads = value->shape[2];
+  d.channels = value->shape[3];
+  d.levels = spatial->shape[0];
+  d.queries = loc->shape[1];
+  d.points = loc->shape[4];
+  require(spatial->shape[1] == 2, "spatial_shapes must have shape (L, 2)");
+  require(start->shape[0] == d.levels, "level_start_index must have shape (L,)");
+  require(loc->shape[0] == d.batch && loc->shape[2] == d.heads && loc->shape[3] == d.levels && loc->shape[5] == 2,
+          "sampling_locations must have shape (B, Lq, Hh, L, P, 2)");
+  require(weight->shape[0] == d.batch && weight->shape[1] == d.queries && weight->shape[2] == d.heads &&
+              weight->shape[3] == d.levels && weight->shape[4] == d.points,
+          "attention_weights must have shape (B, Lq, Hh, L, P)");
+  const int64_t step = d.batch < im2col_step ? d.batch : im2col_step;
+  require(step > 0, "im2col_step chunk must be positive (min(batch, im2col_step) = " + std::to_string(step) + ")");
+  require(d.batch % step == 0, "batch (" + std::to_string(d.batch) + ") must be divisible by im2col_step chunk (" +
+                                   std::to_string(step) + ")");
+  check_dims(d);
+  return d;
+}
+
+msda::DType storage_dtype(const DLTensor* value) {
+  require(value != nullptr, "value is null");
+  if (same_dtype(value->dtype, kDLFloat, 32)) return msda::DType::kF32;
+  if (same_dtype(value->dtype, kDLBfloat, 16)) return msda::DType::kBF16;
+  fail(MSDA_STATUS_INVALID_ARGUMENT, "value must be float32 or bfloat16, got " + dtype_name(value->dtype));
+}
+
+template <typename F>
+int guarded(F&& body) {
+  try {
+    body();
+    g_last_error.clear();
+    return MSDA_STATUS_OK;
+  } catch (const Failure& f) {
+    return f.status;
+  } catch (...) {
+    g_last_error = "internal error";
+    return MSDA_STATUS_CUDA_ERROR;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int ms_deform_attn_forward(const DLTensor* value, const DLTensor* spatial_shapes, const DLTensor* level_start_index,
+                           const DLTensor* sampling_locations, const DLTensor* attention_weights, DLTensor* output,
+                           int im2col_step, void* stream) {
+  return guarded([&] {
+    const msda::DType dt = storage_dtype(value);
+    const uint8_t code = dt == msda::DType::kBF16 ? kDLBfloat : kDLFloat;
+    const uint8_t bits = dt == msda::DType::kBF16 ? 16 : 32;
+    const int dev = value->device.device_id;
+    check_tensor(value, "value", code, bits, 4, dev);
+    check_tensor(spatial_shapes, "spatial_shapes", kDLInt, 64, 2, dev);
+    check_tensor(level_start_index, "level_start_index", kDLInt, 64, 1, dev);
+    check_tensor(sampling_locations, "sampling_locations", code, bits, 6, dev);
+    check_tensor(attention_weights, "attention_weights", code, bits, 5, dev);
+    check_tensor(output, "out", code, bits, 3, dev);
+    const msda_dims_t d =
+        dims_from_views(value, spatial_shapes, level_start_index, sampling_locations, attention_weights, im2col_step);
+    require(output->shape[0] == d.batch && output->shape[1] == d.queries &&
+                output->shape[2] == d.heads * d.channels,
+            "out must have shape (B, Lq, Hh * D)");
+    DeviceGuard guard(dev);
+    msda::Args a{};
+    a.value = data_of(value);
+    a.shapes = static_cast<const int64_t*>(data_of(spatial_shapes));
+    a.starts = static_cast<const int64_t*>(data_of(level_start_index));
+    a.loc = data_of(sampling_locations);
+    a.weight = data_of(attention_weights);
+    a.out = data_of(output);
+    check_launch(msda::launch_forward(dt, to_kernel_dims(d), a, static_cast<cudaStream_t>(stream)),
+                 "ms_deform_attn_forward");
+  });
+}
+
+int ms_deform_attn_backward(const DLTensor* value, const DLTensor* spatial_shapes, const DLTensor* level_start_index,
+                            const DLTensor* sampling_locations, const DLTensor* attention_weights,
+                            const DLTensor* grad_output, DLTensor* grad_value, DLTensor* grad_sampling_loc,
+                            DLTensor* grad_attn_weight, int im2col_step, void* stream) {
+  return guarded([&] {
+    const msda::DType dt = storage_dtype(value);
+    const uint8_t code = dt == msda::DType::kBF16 ? kDLBfloat : kDLFloat;
+    const uint8_t bits = dt == msda::DType::kBF16 ? 16 : 32;
+    const int dev = value->device.device_id;
+    check_tensor(value, "value", code, bits, 4, dev);
+    check_tensor(spatial_shapes, "spatial_shapes", kDLInt, 64, 2, dev);
+    check_tensor(level_start_index, "level_start_index", kDLInt, 64, 1, dev);
+    check_tensor(sampling_locations, "sampling_locations", code, bits, 6, dev);
+    check_tensor(attention_weights, "attention_weights", code, bits, 5, dev);
+    check_tensor(grad_output, "grad", code, bits, 3, dev);
+    check_tensor(grad_value, "grad_value", kDLFloat, 32, 4, dev);
+    check_tensor(grad_sampling_loc, "grad_sampling_locations", kDLFloat, 32, 6, dev);
+    check_tensor(grad_attn_weight, "grad_attention_weights", kDLFloat, 32, 5, dev);
+    const msda_dims_t d =
+        dims_from_views(value, spatial_shapes, level_start_index, sampling_locations, attention_weights, im2col_step);
+    require(grad_output->shape[0] == d.batch && grad_output->shape[1] == d.queries &&
+                grad_output->shape[2] == d.heads * d.channels,
+            "grad must have shape (B, Lq, Hh * D)");
+    for (int i = 0; i < 4; ++i)
+      require(grad_value->shape[i] == value->shape[i], "grad_value must have the shape of value");
+    for (int i = 0; i < 6; ++i)
+      require(grad_sampling_loc->shape[i] == sampling_locations->shape[i],
+              "grad_sampling_locations must have the shape of sampling_locations");
+    for (int i = 0; i < 5; ++i)
+      require(grad_attn_weight->shape[i] == attention_weights->shape[i],
+              "grad_attention_weights must have the shape of attention_weights");
+    DeviceGuard guard(dev);
+    msda::Args a{};
+    a.value = data_of(value);
+    a.shapes = static_cast<const int64_t*>(data_of(spatial_shapes));
+    a.starts = static_cast<const int64_t*>(data_of(level_start_index));
+    a.loc = data_of(sampling_locations);
+    a.weight = data_of(attention_weights);
+    a.grad_out = data_of(grad_output);
+    a.grad_value = static_cast<float*>(data_of(grad_value));
+    a.grad_loc = static_cast<float*>(data_of(grad_sampling_loc));
+    a.grad_weight = static_cast<float*>(data_of(grad_attn_weight));
+    check_launch(msda::launch_backward(dt, to_kernel_dims(d), a, static_cast<cudaStream_t>(stream)),
+                 "ms_deform_attn_backward");
+  });
+}
+
+int msda_forward(msda_dtype_t dtype, const msda_dims_t* dims, const void* value, const int64_t* spatial_shapes,
+                 const int64_t* level_start_index, const void* sampling_locations, const void* attention_weights,
+                 void* output, void* stream) {
+  return guarded([&] {
+    require(dtype == MSDA_DTYPE_FLOAT32 || dtype == MSDA_DTYPE_BFLOAT16, "dtype must be float32 or bfloat16");
+    require(dims != nullptr, "dims is null");
+    check_dims(*dims);
+    const bool empty = dims->batch * dims->queries * dims->heads * dims->channels == 0;
+    require(empty || (value && spatial_shapes && level_start_index && sampling_locations && attention_weights && output),
+            "a required pointer is null");
+    msda::Args a{};
+    a.value = value;
+    a.shapes = spatial_shapes;
+    a.starts = level_start_index;
+    a.loc = sampling_locations;
+    a.weight = attention_weights;
+    a.out = output;
+    const msda::DType dt = dtype == MSDA_DTYPE_BFLOAT16 ? msda::DType::kBF16 : msda::DType::kF32;
+    check_launch(msda::launch_forward(dt, to_kernel_dims(*dims), a, static_cast<cudaStream_t>(stream)),
+                 "msda_forward");
+  });
+}
+
+int msda_backward(msda_dtype_t dtype, const msda_dims_t* dims, const void* value, const int64_t* spatial_shapes,
+                  const int64_t* level_start_index, const void* sampling_locations, const void* attention_weights,
+                  const void* grad_output, float* grad_value, float* grad_sampling_loc, float* grad_attn_weight,
+                  void* stream) {
+  return guarded([&] {
+    require(dtype == MSDA_DTYPE_FLOAT32 || dtype == MSDA_DTYPE_BFLOAT16, "dtype must be float32 or bfloat16");
+    require(dims != nullptr, "dims is null");
+    check_dims(*dims);
+    const bool empty = dims->batch * dims->queries * dims->heads == 0;
+    require(empty || (value && spatial_shapes && level_start_index && sampling_locations && attention_weights &&
+                      grad_output && grad_value && grad_sampling_loc && grad_attn_weight),
+            "a required pointer is null");
+    msda::Args a{};
+    a.value = value;
+    a.shapes = spatial_shapes;
+    a.starts = level_start_index;
+    a.loc = sampling_locations;
+    a.weight = attention_weights;
+    a.grad_out = grad_output;
+    a.grad_value = grad_value;
+    a.grad_loc = grad_sampling_loc;
+    a.grad_weight = grad_attn_weight;
+    const msda::DType dt = dtype == MSDA_DTYPE_BFLOAT16 ? msda::DType::kBF16 : msda::DType::kF32;
+    check_launch(msda::launch_backward(dt, to_kernel_dims(*dims), a, static_cast<cudaStream_t>(stream)),
+                 "msda_backward");
+  });
+}
+
+const char* msda_last_error(void) { return g_last_error.c_str(); }
+
+const char* msda_version(void) { return "0.1.0"; }
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+// Device-side building blocks of the B200 MSDA kernels.
+//
+// Layouts (row-major, contiguous), as muSPACE's MSDA operator defines them
+// (mu_space/ops/multi_scale_deformable_attn.py:26-58):
+//   value               (B, Lin, Hh, D)      storage dtype T (float or bf16)
+//   sampling_locations  (B, Lq, Hh, L, P, 2) T, last dim (x = width, y = height)
+//   attention_weights   (B, Lq, Hh, L, P)    T
+//   output / grad_out   (B, Lq, Hh*D)        T
+//   grad_value          (B, Lin, Hh, D)      fp32, accumulated
+//   grad_loc / grad_w   like loc / weights   fp32, written
+// All arithmetic (geometry, bilinear weights, sums) is fp32 whatever T is.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "msda_kernels.h"
+
+namespace msda {
+
+// ---------------------------------------------------------------------------
+// storage-dtype helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// A (x, y) location pair widened to fp32.
+__device__ __forceinline__ float2 load_loc(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+__device__ __forceinline__ float2 load_loc(const __nv_bfloat16* p) {
+  const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p));
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+// 16 bytes of channels <-> fp32 registers.
+template <typename T>
+struct Vec16;
+
+template <>
+struct Vec16<float> {
+  static constexpr int kLanes = 4;
+  __device__ __forceinline__ static void unpack(const uint4& r, float* f) {
+    f[0] = __uint_as_float(r.x);
+    f[1] = __uint_as_float(r.y);
+    f[2] = __uint_as_float(r.z);
+    f[3] = __uint_as_float(r.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+
+template <>
+struct Vec16<__nv_bfloat16> {
+  static constexpr int kLanes = 8;
+  __device__ __forceinline__ static void unpack(const uint4& r, float* f) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// Streaming read of data used exactly once (locations, weights, grad_out):
+// do not keep it in L1, and let L2 evict it first so the value maps stay.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t policy;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p, uint64_t policy) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(policy));
+  return r;
+}
+
+__device__ __forceinline__ void st16(void* p, const uint4& v) { *reinterpret_cast<uint4*>(p) = v; }
+
+// Vector reduction into fp32 global memory (no return value -> RED, not ATOM).
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// level table
+// ---------------------------------------------------------------------------
+// Stage the (H, W, start) table in shared memory. A level whose rows would fall
+// outside [0, Lin) is emptied (H = W = 0), so a malformed table can never make
+// a kernel read or write outside the value / grad_value buffers.
+__device__ __forceinline__ void stage_levels(Level* table, const int64_t* shapes, const int64_t* starts,
+                                             const Dims& d) {
+  for (int l = threadIdx.x; l < d.levels; l += blockDim.x) {
+    const int64_t h = shapes[2 * l], w = shapes[2 * l + 1], s = starts[l];
+    const bool ok = h > 0 && w > 0 && s >= 0 && h <= (1 << 24) && w <= (1 << 24) && s + h * w <= d.spatial_size;
+    table[l].height = ok ? static_cast<int>(h) : 0;
+    table[l].width = ok ? static_cast<int>(w) : 0;
+    table[l].start = ok ? static_cast<int>(s) : 0;
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// sampling geometry
+// ---------------------------------------------------------------------------
+// grid_sample(align_corners=False) maps a location in [0, 1] to a pixel
+// coordinate as ((2 * loc - 1) + 1) * (size / 2) - 0.5, every step rounded to
+// fp32 on its own; the _rn intrinsics keep the compiler from fusing steps, so
+// the four corners and their weights equal the reference's bit for bit.
+__device__ __forceinline__ float unnormalize(float loc, float half_size) {
+  const float g = __fsub_rn(__fmul_rn(2.0f, loc), 1.0f);
+  return __fsub_rn(__fmul_rn(__fadd_rn(g, 1.0f), half_size), 0.5f);
+}
+
+// One bilinear sample: the four corner rows (pixel index inside the batch's
+// value map, or -1 when the corner is outside the level) and their weights.
+struct Corners {
+  int row[4];  // pixel index, -1 = zero padding
+  float w[4];  // bilinear weights hh*hw, hh*lw, lh*hw, lh*lw
+  float lh, lw, hh, hw;
+};
+
+// Returns false when no corner can be inside the level (or the coordinate is
+// not finite); the sample then contributes nothing and has zero gradients.
+__device__ __forceinline__ bool corners(const Level& lv, float loc_x, float loc_y, Corners& c) {
+  const float fh = static_cast<float>(lv.height), fw = static_cast<float>(lv.width);
+  const float y = unnormalize(loc_y, 0.5f * fh);
+  const float x = unnormalize(loc_x, 0.5f * fw);
+  if (!(y > -2.0f && x > -2.0f && y < fh + 1.0f && x < fw + 1.0f)) return false;
+  const float yf = floorf(y), xf = floorf(x);
+  const int y0 = static_cast<int>(yf), x0 = static_cast<int>(xf);
+  c.lh = __fsub_rn(y, yf);
+  c.lw = __fsub_rn(x, xf);
+  c.hh = __fsub_rn(1.0f, c.lh);
+  c.hw = __fsub_rn(1.0f, c.lw);
+  const bool y0ok = y0 >= 0 && y0 < lv.height, y1ok = y0 + 1 >= 0 && y0 + 1 < lv.height;
+  const bool x0ok = x0 >= 0 && x0 < lv.width, x1ok = x0 + 1 >= 0 && x0 + 1 < lv.width;
+  const int base = lv.start + y0 * lv.width + x0;
+  c.row[0] = (y0ok && x0ok) ? base : -1;
+  c.row[1] = (y0ok && x1ok) ? base + 1 : -1;
+  c.row[2] = (y1ok && x0ok) ? base + lv.width : -1;
+  c.row[3] = (y1ok && x1ok) ? base + lv.width + 1 : -1;
+  c.w[0] = __fmul_rn(c.hh, c.hw);
+  c.w[1] = __fmul_rn(c.hh, c.lw);
+  c.w[2] = __fmul_rn(c.lh, c.hw);
+  c.w[3] = __fmul_rn(c.lh, c.lw);
+  return true;
+}
+
+}  // namespace msda

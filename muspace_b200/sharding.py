@@ -1,0 +1,108 @@
+"""Multi-GPU sharding of the MSDA work (one process per GPU, ``torch.distributed``).
+
+The reference has no multi-GPU logic on this path; this module adds the two
+decompositions the B200 build runs.
+
+* Batch x camera sharding. Every (b, q, h) head-row of the forward and every
+  sample of the backward only touches the value map of its own batch entry, so
+  a rank that owns batch entries ``[b0, b1)`` needs nothing from any other
+  rank: no collective is on the data path (``shard_range`` picks the slice).
+
+* Query sharding for batch-size-1 training (one 6-camera sample). The value
+  maps are replicated, each rank runs the forward and backward on its own
+  query range ``[q0, q1)``; forward outputs, ``grad_sampling_locations`` and
+  ``grad_attention_weights`` stay local, while ``grad_value`` is a sum over all
+  queries, so the partial fp32 sums are reduce-scattered
+  (``torch.distributed.reduce_scatter_tensor``, NCCL over NVLink / NVSwitch)
+  and each rank ends up owning one contiguous slice of the summed gradient.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Balanced contiguous ``[start, stop)`` of ``n`` units for ``rank`` of ``world``."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def padded_numel(numel: int, world: int) -> int:
+    return -(-numel // world) * world
+
+
+def reduce_scatter_grad_value(partial: torch.Tensor, group=None) -> tuple[torch.Tensor, int]:
+    """Sum ``partial`` (this rank's fp32 grad_value over its queries) across the
+    group; return this rank's slice of the sum and the slice's flat offset.
+
+    ``partial`` is flattened and zero-padded to a multiple of the world size so
+    every rank's slice has the same length (NCCL's reduce-scatter contract).
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    flat = partial.reshape(-1)
+    total = padded_numel(flat.numel(), world)
+    if total != flat.numel():
+        flat = torch.nn.functional.pad(flat, (0, total - flat.numel()))
+    shard = torch.empty(total // world, dtype=flat.dtype, device=flat.device)
+    dist.reduce_scatter_tensor(shard, flat, op=dist.ReduceOp.SUM, group=group)
+    return shard, rank * (total // world)
+
+
+def all_gather_grad_value(shard: torch.Tensor, shape, group=None) -> torch.Tensor:
+    """Inverse of :func:`reduce_scatter_grad_value`: the full summed tensor."""
+    world = dist.get_world_size(group)
+    full = torch.empty(shard.numel() * world, dtype=shard.dtype, device=shard.device)
+    dist.all_gather_into_tensor(full, shard, group=group)
+    numel = 1
+    for s in shape:
+        numel *= int(s)
+    return full[:numel].view(*shape)
+
+
+class QueryShardedStep:
+    """One forward + backward of the bs=1 query-sharded form on this rank.
+
+    ``inp`` holds the whole problem (value replicated on every rank); the rank
+    keeps contiguous copies of its query slice of the locations, weights and
+    incoming gradient, runs the two C-ABI calls on them and reduce-scatters
+    the fp32 ``grad_value``.
+    """
+
+    def __init__(self, inp: dict, dtype: torch.dtype, rank: int, world: int):
+        from .runtime.native import native_function
+
+        self.fwd = native_function("ms_deform_attn_forward")
+        self.bwd = native_function("ms_deform_attn_backward")
+        self.world = world
+        queries = inp["sampling_locations"].shape[1]
+        self.q0, self.q1 = shard_range(queries, world, rank)
+        sl = slice(self.q0, self.q1)
+        self.value = inp["value"]
+        self.shapes = inp["spatial_shapes"]
+        self.start = inp["level_start_index"]
+        self.loc = inp["sampling_locations"][:, sl].contiguous()
+        self.weight = inp["attention_weights"][:, sl].contiguous()
+        self.grad_out = inp["grad_output"][:, sl].contiguous()
+        device = self.value.device
+        self.out = torch.empty(self.grad_out.shape, dtype=dtype, device=device)
+        self.gv = torch.zeros(self.value.shape, dtype=torch.float32, device=device)
+        self.gl = torch.empty(self.loc.shape, dtype=torch.float32, device=device)
+        self.gw = torch.empty(self.weight.shape, dtype=torch.float32, device=device)
+        self.shard = None
+
+    def __call__(self):
+        args = (self.value, self.shapes, self.start, self.loc, self.weight)
+        self.fwd(*args, self.out, 64)
+        self.gv.zero_()
+        self.bwd(*args, self.grad_out, self.gv, self.gl, self.gw, 64)
+        if self.world > 1:
+            self.shard, _ = reduce_scatter_grad_value(self.gv)
+        else:
+            self.shard = self.gv.view(-1)
+        return self.shard
