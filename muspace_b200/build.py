@@ -21,7 +21,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 INCLUDE = PACKAGE.parent / "include"
 LIBRARY = PACKAGE / "native" / "libmuspace_ops.so"
-SOURCES = ("msda_capi.cpp", "msda_forward.cu", "msda_backward.cu")
+SOURCES = ("msda_capi.cpp", "msda_forward.cu", "msda_backward.cu", "msda_bucketed.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 
@@ -49,12 +49,18 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= built for p in _inputs())
 
 
-def build_native(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the MSDA library (skipped when it is newer than every source)."""
-    if not force and up_to_date():
+def build_native(force: bool = False, verbose: bool = False, output: Path | None = None,
+                 defines: tuple[str, ...] = ()) -> Path:
+    """Compile the MSDA library (skipped when it is newer than every source).
+
+    ``output`` and ``defines`` (``NAME=VALUE`` macro overrides of the tuning
+    constants) build a variant elsewhere; the default builds the package's own.
+    """
+    target = Path(output) if output is not None else LIBRARY
+    if output is None and not defines and not force and up_to_date():
         return LIBRARY
-    LIBRARY.parent.mkdir(parents=True, exist_ok=True)
-    tmp = LIBRARY.with_suffix(".so.tmp")
+    target.parent.mkdir(parents=True, exist_ok=True)
+    tmp = target.with_suffix(".so.tmp")
     cmd = [
         nvcc(),
         *ARCH_FLAGS,
@@ -66,7 +72,10 @@ def build_native(force: bool = False, verbose: bool = False) -> Path:
         "-fPIC,-fvisibility=hidden",
         "-cudart",
         "static",
+        "-Xlinker",
+        "--no-undefined",
         f"-I{INCLUDE}",
+        *(f"-D{d}" for d in defines),
         *(str(CSRC / s) for s in SOURCES),
         "-o",
         str(tmp),
@@ -75,8 +84,8 @@ def build_native(force: bool = False, verbose: bool = False) -> Path:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
-    tmp.replace(LIBRARY)
-    return LIBRARY
+    tmp.replace(target)
+    return target
 
 
 def main() -> None:

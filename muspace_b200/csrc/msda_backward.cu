@@ -25,22 +25,17 @@
 
 namespace msda {
 
-template <int G>
-__device__ __forceinline__ float group_sum(float v) {
-#pragma unroll
-  for (int m = G / 2; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m, G);
-  return v;
-}
 
 template <typename T, int G>
-__global__ void __launch_bounds__(256) backward_vec_kernel(Dims d, const T* __restrict__ value,
+__global__ void __launch_bounds__(256, 3) backward_vec_kernel(Dims d, const T* __restrict__ value,
                                                            const int64_t* __restrict__ shapes,
                                                            const int64_t* __restrict__ starts,
                                                            const T* __restrict__ loc, const T* __restrict__ weight,
                                                            const T* __restrict__ grad_out,
                                                            float* __restrict__ grad_value,
                                                            float* __restrict__ grad_loc,
-                                                           float* __restrict__ grad_weight) {
+                                                           float* __restrict__ grad_weight,
+                                                           const int* __restrict__ order) {
   using V = Vec16<T>;
   constexpr int kVec = V::kLanes;
   extern __shared__ Level levels[];
@@ -59,17 +54,22 @@ __global__ void __launch_bounds__(256) backward_vec_kernel(Dims d, const T* __re
   for (int64_t item = static_cast<int64_t>(blockIdx.x) * groups_per_cta + threadIdx.x / G;
        item - (threadIdx.x % 32) / G < items; item += stride) {
     const bool live = item < items;
-    const int64_t it = live ? item : items - 1;
+    const int64_t slot = live ? item : items - 1;
+    const int64_t it = order ? order[slot] : slot;
     const int h = static_cast<int>(it % d.heads);
     const int64_t b = it / (static_cast<int64_t>(d.queries) * d.heads);
-    const int64_t vrow0 = (b * d.spatial_size) * row_stride + h * d.channels + sub * kVec;
-    const T* vbase = value + vrow0;
-    float* gbase = grad_value + vrow0;
+    const int64_t head0 = (b * d.spatial_size) * row_stride + h * d.channels;
+    const T* vbase = value + head0 + sub * kVec;
+    float* gbase = grad_value + head0;
     const T* lp = loc + it * samples * 2;
     const T* wp = weight + it * samples;
 
-    float g[kVec];
-    V::unpack(ld_stream16(grad_out + it * d.channels + sub * kVec, evict_first_policy()), g);
+    // g in the lane's 16-byte load slice (for the dot products) and in the
+    // slice it scatters (for grad_value); see RedSlice.
+    float g[kVec], gr[kVec];
+    const T* grow = grad_out + it * d.channels;
+    V::unpack(ld_stream16(grow + sub * kVec, evict_first_policy()), g);
+    RedSlice<T, G>::load(grow, sub, g, gr);
 
     for (int l = 0; l < d.levels; ++l) {
       const Level lv = levels[l];
@@ -101,11 +101,7 @@ __global__ void __launch_bounds__(256) backward_vec_kernel(Dims d, const T* __re
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             if (c.row[k] < 0) continue;
-            const float wa = c.w[k] * a;
-            float* dst = gbase + static_cast<int64_t>(c.row[k]) * row_stride;
-#pragma unroll
-            for (int i = 0; i < kVec; i += 4)
-              red_add_v4(dst + i, wa * g[i], wa * g[i + 1], wa * g[i + 2], wa * g[i + 3]);
+            RedSlice<T, G>::scatter(gbase + static_cast<int64_t>(c.row[k]) * row_stride, sub, c.w[k] * a, gr);
           }
         }
         part_w = group_sum<G>(part_w);
@@ -187,7 +183,8 @@ static cudaError_t launch_backward_vec(const Dims& d, const Args& a, cudaStream_
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
   backward_vec_kernel<T, G><<<grid, kThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
-      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight);
+      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight,
+      a.order);
   return cudaGetLastError();
 }
 
@@ -212,7 +209,7 @@ static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t 
   return cudaGetLastError();
 }
 
-cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
+cudaError_t launch_backward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
   if (d.batch == 0 || d.queries == 0 || d.heads == 0) return cudaSuccess;
   return dtype == DType::kBF16 ? launch_backward_t<__nv_bfloat16>(d, a, stream)
                                : launch_backward_t<float>(d, a, stream);

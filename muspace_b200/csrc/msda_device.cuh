@@ -103,6 +103,25 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p, uint64_t policy) {
 
 __device__ __forceinline__ void st16(void* p, const uint4& v) { *reinterpret_cast<uint4*>(p) = v; }
 
+// Two independent fp32 FMAs in one instruction (sm_100 fma.rn.f32x2); each
+// lane rounds exactly like fmaf.
+union F2 {
+  float2 f;
+  unsigned long long u;
+};
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  F2 x, y, z, r;
+  x.f = a;
+  y.f = b;
+  z.f = c;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.u) : "l"(x.u), "l"(y.u), "l"(z.u));
+  return r.f;
+}
+// A 32-bit word of two bf16 channels as (low channel, high channel) in fp32.
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 // Vector reduction into fp32 global memory (no return value -> RED, not ATOM).
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
@@ -173,5 +192,54 @@ __device__ __forceinline__ bool corners(const Level& lv, float loc_x, float loc_
   c.w[3] = __fmul_rn(c.lh, c.lw);
   return true;
 }
+
+// ---------------------------------------------------------------------------
+// lane-group reductions and gradient scatter
+// ---------------------------------------------------------------------------
+// Sum over the G lanes of a group (G a power of two <= 32, groups aligned).
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int m = G / 2; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m, G);
+  return v;
+}
+
+// Which fp32 channels a lane scatters into grad_value. A vector RED moves 16
+// bytes per lane, and the L2 processes reductions per 32-byte sector, so one
+// RED instruction of the group should cover whole sectors. With fp32 storage
+// the lane's load slice (4 channels, lanes side by side) already does. With
+// bf16 storage a lane loads 8 channels (16 bytes), which are 32 bytes of fp32:
+// scattering them itself would touch every sector with two half-filled REDs.
+// Instead lane j scatters channels [4j, 4j+4) and [4G+4j, 4G+4j+4), so each
+// RED instruction of the group fills 16G contiguous bytes.
+template <typename T, int G>
+struct RedSlice {
+  __device__ __forceinline__ static void load(const T*, int, const float* g, float* gr) {
+#pragma unroll
+    for (int i = 0; i < Vec16<T>::kLanes; ++i) gr[i] = g[i];
+  }
+  __device__ __forceinline__ static void scatter(float* head_row, int sub, float wa, const float* gr) {
+    float* dst = head_row + sub * 4;
+    red_add_v4(dst, wa * gr[0], wa * gr[1], wa * gr[2], wa * gr[3]);
+  }
+};
+
+template <int G>
+struct RedSlice<__nv_bfloat16, G> {
+  __device__ __forceinline__ static void load(const __nv_bfloat16* grow, int sub, const float*, float* gr) {
+    const uint2 lo = __ldg(reinterpret_cast<const uint2*>(grow + 4 * sub));
+    const uint2 hi = __ldg(reinterpret_cast<const uint2*>(grow + 4 * G + 4 * sub));
+    const uint32_t w[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      gr[2 * i] = __uint_as_float(w[i] << 16);
+      gr[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ __forceinline__ static void scatter(float* head_row, int sub, float wa, const float* gr) {
+    red_add_v4(head_row + 4 * sub, wa * gr[0], wa * gr[1], wa * gr[2], wa * gr[3]);
+    red_add_v4(head_row + 4 * G + 4 * sub, wa * gr[4], wa * gr[5], wa * gr[6], wa * gr[7]);
+  }
+};
 
 }  // namespace msda

@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(256) forward_vec_kernel(Dims d, const T* __res
                                                           const int64_t* __restrict__ shapes,
                                                           const int64_t* __restrict__ starts,
                                                           const T* __restrict__ loc, const T* __restrict__ weight,
-                                                          T* __restrict__ out) {
+                                                          T* __restrict__ out, const int* __restrict__ order) {
   using V = Vec16<T>;
   constexpr int kVec = V::kLanes;
   extern __shared__ Level levels[];
@@ -38,17 +38,19 @@ __global__ void __launch_bounds__(256) forward_vec_kernel(Dims d, const T* __res
   const int row_stride = d.heads * d.channels;  // elements between neighbouring pixels
   const int samples = d.levels * d.points;
 
-  for (int64_t item = static_cast<int64_t>(blockIdx.x) * groups_per_cta + threadIdx.x / G; item < items;
-       item += static_cast<int64_t>(gridDim.x) * groups_per_cta) {
+  for (int64_t slot = static_cast<int64_t>(blockIdx.x) * groups_per_cta + threadIdx.x / G; slot < items;
+       slot += static_cast<int64_t>(gridDim.x) * groups_per_cta) {
+    const int64_t item = order ? order[slot] : slot;
     const int h = static_cast<int>(item % d.heads);
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
     const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kVec;
     const T* lp = loc + item * samples * 2;
     const T* wp = weight + item * samples;
 
-    float acc[kVec];
+    // channel pairs accumulate with packed fp32x2 FMAs: acc += (w_k a) v_k
+    float2 acc[kVec / 2];
 #pragma unroll
-    for (int i = 0; i < kVec; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kVec / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
 
     for (int l = 0; l < d.levels; ++l) {
       const Level lv = levels[l];
@@ -63,17 +65,27 @@ __global__ void __launch_bounds__(256) forward_vec_kernel(Dims d, const T* __res
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           raw[k] = c.row[k] >= 0 ? ldg16(vbase + static_cast<int64_t>(c.row[k]) * row_stride) : make_uint4(0, 0, 0, 0);
-        float v[4][kVec];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) V::unpack(raw[k], v[k]);
+        for (int k = 0; k < 4; ++k) {
+          const float wk = c.w[k] * a;
+          const float2 w2 = make_float2(wk, wk);
+          const uint32_t words[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
 #pragma unroll
-        for (int i = 0; i < kVec; ++i) {
-          const float bil = c.w[0] * v[0][i] + c.w[1] * v[1][i] + c.w[2] * v[2][i] + c.w[3] * v[3][i];
-          acc[i] = fmaf(bil, a, acc[i]);
+          for (int i = 0; i < kVec / 2; ++i) {
+            const float2 v2 = sizeof(T) == 2 ? bf16x2_to_float2(words[i])
+                                             : make_float2(__uint_as_float(words[2 * i]), __uint_as_float(words[2 * i + 1]));
+            acc[i] = ffma2(v2, w2, acc[i]);
+          }
         }
       }
     }
-    st16(out + item * d.channels + sub * kVec, V::pack(acc));
+    float flat[kVec];
+#pragma unroll
+    for (int i = 0; i < kVec / 2; ++i) {
+      flat[2 * i] = acc[i].x;
+      flat[2 * i + 1] = acc[i].y;
+    }
+    st16(out + item * d.channels + sub * kVec, V::pack(flat));
   }
 }
 
@@ -127,7 +139,7 @@ static cudaError_t launch_forward_vec(const Dims& d, const Args& a, cudaStream_t
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
   forward_vec_kernel<T, G><<<grid, kThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
-      static_cast<const T*>(a.weight), static_cast<T*>(a.out));
+      static_cast<const T*>(a.weight), static_cast<T*>(a.out), a.order);
   return cudaGetLastError();
 }
 
@@ -153,7 +165,7 @@ static cudaError_t launch_forward_t(const Dims& d, const Args& a, cudaStream_t s
   return cudaGetLastError();
 }
 
-cudaError_t launch_forward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
+cudaError_t launch_forward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
   if (d.batch == 0 || d.queries == 0 || d.heads == 0 || d.channels == 0) return cudaSuccess;
   return dtype == DType::kBF16 ? launch_forward_t<__nv_bfloat16>(d, a, stream) : launch_forward_t<float>(d, a, stream);
 }

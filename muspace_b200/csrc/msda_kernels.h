@@ -30,6 +30,7 @@ struct Args {
   float* grad_value;
   float* grad_loc;
   float* grad_weight;
+  const int* order;  // optional head-row visiting order (row-wise kernels); null = natural
 };
 
 // Grid-stride kernels never need more CTAs than this; 148 SMs x 8 resident
@@ -56,7 +57,14 @@ inline int vec_group(int channels, size_t elem, const Args& a) {
   return static_cast<int>(g);
 }
 
+// Entry points used by the C-ABI: pick the tiled path when it applies and
+// fall back to the row-wise kernels otherwise (msda_tiled.cu).
 cudaError_t launch_forward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
+
+// Row-wise kernels: one item per lane group in natural (b, q, h) order; any
+// channel count (msda_forward.cu, msda_backward.cu).
+cudaError_t launch_forward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
+cudaError_t launch_backward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 
 }  // namespace msda

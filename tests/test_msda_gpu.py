@@ -89,7 +89,7 @@ def test_bf16_storage_matches_fp32_reference(cuda_device, name):
     _close(gw, exp_gw, BF16_TOL, f"{name}:grad_w")
 
 
-@pytest.mark.parametrize("name", ["c1_small", "c3_small", "ragged_d16", "odd_d5", "wide_d64", "edges"])
+@pytest.mark.parametrize("name", ["c1_small", "c3_small", "ragged_d16", "odd_d5", "wide_d64", "edges", "ref_fixture_c"])
 def test_c_abi_matches_c_oracle(cuda_device, name):
     """Straight through the DLPack C-ABI (no autograd), both dtypes."""
     g = load_golden(name)
