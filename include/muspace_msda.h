@@ -153,6 +153,39 @@ MSDA_API int msda_backward(msda_dtype_t dtype, const msda_dims_t *dims, const vo
                   const void *attention_weights, const void *grad_output, float *grad_value,
                   float *grad_sampling_loc, float *grad_attn_weight, void *stream);
 
+/*
+ * msda_backward without any device allocation. No counterpart in the
+ * reference: this entry point exists for callers that may not allocate GPU
+ * memory once they run, such as deployments that plan all device memory
+ * before start-up and forbid allocation afterwards (automotive and other
+ * real-time inference runtimes), and plugin hosts that own the device memory
+ * and do not let a plugin call the CUDA allocator.
+ *
+ * Same arguments, layouts and results as msda_backward (grad_value is
+ * accumulated into, so the caller zeroes it). The work space that
+ * msda_backward takes from the stream-ordered allocator comes instead from one
+ * fixed 8 MiB array in device memory that this library declares; every GPU
+ * that loads the library keeps it until the process exits. It is enough for
+ * about one million head-rows (B * Lq * Hh); larger calls are rejected with
+ * MSDA_STATUS_INVALID_ARGUMENT and nothing runs. The function allocates
+ * nothing: no cudaMalloc, cudaMallocAsync, cudaFree, no allocating library.
+ *
+ * The array is shared by every call on a device and keeps the last call's
+ * contents; each call clears what must start at zero. Calls whose work
+ * overlaps on the GPU (different streams, or different host threads on one
+ * device without ordering between them) race on the array: order them on one
+ * stream, or synchronise between them.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current) and caches it; make that first call before capturing any
+ * stream on that device.
+ */
+MSDA_API int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t *dims, const void *value,
+                                          const int64_t *spatial_shapes, const int64_t *level_start_index,
+                                          const void *sampling_locations, const void *attention_weights,
+                                          const void *grad_output, float *grad_value, float *grad_sampling_loc,
+                                          float *grad_attn_weight, void *stream);
+
 /* Message of the last failed call on this thread ("" after a success). The
  * reference raised it as a TVM-FFI exception (csrc/ffi/tensor_utils.hpp:13-34). */
 MSDA_API const char *msda_last_error(void);

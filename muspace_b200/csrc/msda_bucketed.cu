@@ -753,4 +753,18 @@ cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStrea
   return dispatch(false, dtype, d, a, stream);
 }
 
+size_t backward_scratch_bytes(DType dtype, const Dims& d, const Args& a) {
+  if (d.batch == 0 || d.queries == 0 || d.heads == 0) return 0;
+  return bucketed_lanes(d, dtype == DType::kBF16 ? 2 : 4, a) != 0 ? plan_bytes(d) : 0;
+}
+
+cudaError_t launch_backward_on_scratch(DType dtype, const Dims& d, const Args& a, void* scratch, cudaStream_t stream) {
+  if (d.batch == 0 || d.queries == 0 || d.heads == 0) return cudaSuccess;
+  const int lpc = bucketed_lanes(d, dtype == DType::kBF16 ? 2 : 4, a);
+  if (lpc == 0) return launch_backward_rowwise(dtype, d, a, stream);
+  const BucketPlan plan = carve(scratch, d);
+  return dtype == DType::kBF16 ? run_bucketed<__nv_bfloat16>(false, d, a, lpc, plan, stream)
+                               : run_bucketed<float>(false, d, a, lpc, plan, stream);
+}
+
 }  // namespace msda

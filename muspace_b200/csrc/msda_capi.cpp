@@ -290,6 +290,43 @@ int msda_backward(msda_dtype_t dtype, const msda_dims_t* dims, const void* value
   });
 }
 
+int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t* dims, const void* value,
+                                 const int64_t* spatial_shapes, const int64_t* level_start_index,
+                                 const void* sampling_locations, const void* attention_weights,
+                                 const void* grad_output, float* grad_value, float* grad_sampling_loc,
+                                 float* grad_attn_weight, void* stream) {
+  return guarded([&] {
+    require(dtype == MSDA_DTYPE_FLOAT32 || dtype == MSDA_DTYPE_BFLOAT16, "dtype must be float32 or bfloat16");
+    require(dims != nullptr, "dims is null");
+    check_dims(*dims);
+    const bool empty = dims->batch * dims->queries * dims->heads == 0;
+    require(empty || (value && spatial_shapes && level_start_index && sampling_locations && attention_weights &&
+                      grad_output && grad_value && grad_sampling_loc && grad_attn_weight),
+            "a required pointer is null");
+    msda::Args a{};
+    a.value = value;
+    a.shapes = spatial_shapes;
+    a.starts = level_start_index;
+    a.loc = sampling_locations;
+    a.weight = attention_weights;
+    a.grad_out = grad_output;
+    a.grad_value = grad_value;
+    a.grad_loc = grad_sampling_loc;
+    a.grad_weight = grad_attn_weight;
+    const msda::DType dt = dtype == MSDA_DTYPE_BFLOAT16 ? msda::DType::kBF16 : msda::DType::kF32;
+    const msda::Dims kd = to_kernel_dims(*dims);
+    const size_t need = msda::backward_scratch_bytes(dt, kd, a);
+    require(need <= msda::static_scratch_capacity(),
+            "problem needs " + std::to_string(need) + " bytes of scratch, the static scratch holds " +
+                std::to_string(msda::static_scratch_capacity()) +
+                " (about 1M head-rows B * Lq * Hh); use msda_backward for larger calls");
+    void* scratch = nullptr;
+    if (need > 0) check_launch(msda::static_scratch_address(&scratch), "static scratch set-up");
+    check_launch(msda::launch_backward_on_scratch(dt, kd, a, scratch, static_cast<cudaStream_t>(stream)),
+                 "msda_backward_static_scratch");
+  });
+}
+
 const char* msda_last_error(void) { return g_last_error.c_str(); }
 
 const char* msda_version(void) { return "0.1.0"; }

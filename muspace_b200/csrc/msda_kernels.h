@@ -62,6 +62,16 @@ inline int vec_group(int channels, size_t elem, const Args& a) {
 cudaError_t launch_forward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 
+// Backward on caller-provided scratch (used by the static-scratch entry point):
+// the scratch bytes the call needs (0 when the bucketed kernels do not apply
+// and the scratch-free row-wise kernels run instead), and the launch itself.
+size_t backward_scratch_bytes(DType dtype, const Dims& d, const Args& a);
+cudaError_t launch_backward_on_scratch(DType dtype, const Dims& d, const Args& a, void* scratch, cudaStream_t stream);
+
+// The fixed per-device scratch array (msda_noalloc.cu).
+size_t static_scratch_capacity();
+cudaError_t static_scratch_address(void** out);
+
 // Row-wise kernels: one item per lane group in natural (b, q, h) order; any
 // channel count (msda_forward.cu, msda_backward.cu).
 cudaError_t launch_forward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);

@@ -98,3 +98,17 @@ def test_plain_pointer_entry_validates_sizes():
     # an empty problem launches nothing and succeeds
     assert _plain_forward(_Dims(0, 4, 1, 4, 1, 1, 1)) == 0
     assert module.last_error() == ""
+
+
+def test_static_scratch_backward_rejects_problems_beyond_its_array():
+    """The no-allocation backward refuses, on the host and before any CUDA
+    call, a problem whose work space exceeds its fixed array (c4: 3.84 M
+    head-rows). The pointers are never touched on this path."""
+    lib = native.load_native_module().lib
+    fn = lib.msda_backward_static_scratch
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int, ctypes.POINTER(_Dims)] + [ctypes.c_void_p] * 10
+    dims = _Dims(48, 30825, 8, 32, 4, 10000, 8)
+    aligned = ctypes.c_void_p(256)  # never dereferenced: the size check fails first
+    assert fn(1, ctypes.byref(dims), *([aligned] * 9), None) == 1
+    assert "bytes of scratch" in native.load_native_module().last_error()
