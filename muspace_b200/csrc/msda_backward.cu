@@ -19,14 +19,17 @@
 // scatters its 16-byte channel slice of every in-bounds corner with
 // red.global.add.v4.f32 (one vector reduction per 4 channels, no return
 // value), so a bf16 D=32 corner costs 8 vector REDs instead of 32 scalar
-// atomics. The three per-sample dot products are reduced across the group with
-// xor shuffles and one lane stores them.
+// atomics. Per sample and corner k each lane forms T_k = sum_c g_c v_k,c over
+// its channels (packed fp32x2 FMAs); xor shuffles sum the four T_k over the
+// group and one lane derives grad_w and grad_loc from them.
 #include "msda_device.cuh"
 
 namespace msda {
 
 
-template <typename T, int G>
+// kScatter = false computes grad_loc / grad_w only; grad_value then comes from
+// the bucketed scatter kernel (msda_bucketed.cu).
+template <typename T, int G, bool kScatter>
 __global__ void __launch_bounds__(256, 3) backward_vec_kernel(Dims d, const T* __restrict__ value,
                                                            const int64_t* __restrict__ shapes,
                                                            const int64_t* __restrict__ starts,
@@ -64,12 +67,15 @@ __global__ void __launch_bounds__(256, 3) backward_vec_kernel(Dims d, const T* _
     const T* lp = loc + it * samples * 2;
     const T* wp = weight + it * samples;
 
-    // g in the lane's 16-byte load slice (for the dot products) and in the
-    // slice it scatters (for grad_value); see RedSlice.
+    // g in the lane's 16-byte load slice (for the dot products, as channel
+    // pairs) and in the slice it scatters (for grad_value); see RedSlice.
     float g[kVec], gr[kVec];
     const T* grow = grad_out + it * d.channels;
     V::unpack(ld_stream16(grow + sub * kVec, evict_first_policy()), g);
     RedSlice<T, G>::load(grow, sub, g, gr);
+    float2 g2[kVec / 2];
+#pragma unroll
+    for (int i = 0; i < kVec / 2; ++i) g2[i] = make_float2(g[2 * i], g[2 * i + 1]);
 
     for (int l = 0; l < d.levels; ++l) {
       const Level lv = levels[l];
@@ -79,39 +85,49 @@ __global__ void __launch_bounds__(256, 3) backward_vec_kernel(Dims d, const T* _
         const float2 xy = load_loc(lp + 2 * s);
         const float a = to_f32(wp[s]);
         Corners c;
-        float part_w = 0.0f, part_x = 0.0f, part_y = 0.0f;
-        if (live && corners(lv, xy.x, xy.y, c)) {
+        // T_k = sum_c g_c v_k,c over this lane's channels, one per corner k
+        float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const bool valid = live && corners(lv, xy.x, xy.y, c);
+        if (valid) {
           uint4 raw[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             raw[k] = c.row[k] >= 0 ? ldg16(vbase + static_cast<int64_t>(c.row[k]) * row_stride)
                                    : make_uint4(0, 0, 0, 0);
-          float v[4][kVec];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) V::unpack(raw[k], v[k]);
-#pragma unroll
-          for (int i = 0; i < kVec; ++i) {
-            const float bil = c.w[0] * v[0][i] + c.w[1] * v[1][i] + c.w[2] * v[2][i] + c.w[3] * v[3][i];
-            const float dx = c.hh * (v[1][i] - v[0][i]) + c.lh * (v[3][i] - v[2][i]);
-            const float dy = c.hw * (v[2][i] - v[0][i]) + c.lw * (v[3][i] - v[1][i]);
-            part_w = fmaf(g[i], bil, part_w);
-            part_x = fmaf(g[i], dx, part_x);
-            part_y = fmaf(g[i], dy, part_y);
-          }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            if (c.row[k] < 0) continue;
-            RedSlice<T, G>::scatter(gbase + static_cast<int64_t>(c.row[k]) * row_stride, sub, c.w[k] * a, gr);
+            const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+            float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int i = 0; i < kVec / 2; ++i) {
+              const float2 v2 = sizeof(T) == 2 ? bf16x2_to_float2(w[i])
+                                               : make_float2(__uint_as_float(w[2 * i]), __uint_as_float(w[2 * i + 1]));
+              acc = ffma2(g2[i], v2, acc);
+            }
+            t[k] = acc.x + acc.y;
+          }
+          if (kScatter) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if (c.row[k] < 0) continue;
+              RedSlice<T, G>::scatter(gbase + static_cast<int64_t>(c.row[k]) * row_stride, sub, c.w[k] * a, gr);
+            }
           }
         }
-        part_w = group_sum<G>(part_w);
-        part_x = group_sum<G>(part_x);
-        part_y = group_sum<G>(part_y);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) t[k] = group_sum<G>(t[k]);
         if (live && sub == 0) {
+          // grad_w = sum_k w_k T_k; grad_x = W a (hh (T_01 - T_00) + lh (T_11 - T_10));
+          // grad_y = H a (hw (T_10 - T_00) + lw (T_11 - T_01)); zero for a skipped sample
+          float gw = 0.0f, gx = 0.0f, gy = 0.0f;
+          if (valid) {
+            gw = c.w[0] * t[0] + c.w[1] * t[1] + c.w[2] * t[2] + c.w[3] * t[3];
+            gx = static_cast<float>(lv.width) * a * (c.hh * (t[1] - t[0]) + c.lh * (t[3] - t[2]));
+            gy = static_cast<float>(lv.height) * a * (c.hw * (t[2] - t[0]) + c.lw * (t[3] - t[1]));
+          }
           const int64_t so = it * samples + s;
-          grad_weight[so] = part_w;
-          *reinterpret_cast<float2*>(grad_loc + 2 * so) =
-              make_float2(static_cast<float>(lv.width) * part_x * a, static_cast<float>(lv.height) * part_y * a);
+          grad_weight[so] = gw;
+          *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(gx, gy);
         }
       }
     }
@@ -181,7 +197,8 @@ static cudaError_t launch_backward_vec(const Dims& d, const Args& a, cudaStream_
   const int64_t groups_per_cta = kThreads / G;
   const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
-  backward_vec_kernel<T, G><<<grid, kThreads, level_smem(d), stream>>>(
+  auto kernel = a.skip_grad_value ? backward_vec_kernel<T, G, false> : backward_vec_kernel<T, G, true>;
+  kernel<<<grid, kThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight,
       a.order);
@@ -199,6 +216,7 @@ static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t 
     case 32: return launch_backward_vec<T, 32>(d, a, stream);
     default: break;
   }
+  if (a.skip_grad_value) return cudaErrorInvalidValue;  // the scalar kernel always scatters
   constexpr int kThreads = 256;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int64_t blocks = (items + kThreads - 1) / kThreads;

@@ -1,33 +1,28 @@
-// Bucketed MSDA: head-rows grouped by where they sample; per-sample geometry
-// staged once in shared memory; the backward's grad_value scatter combined
-// per bilinear cell before it reaches L2.
+// grad_value for the MSDA backward, and the dispatch of both directions.
 //
 // Why. A BEVFormer-base SCA call (6 cameras, 10000 queries, 8 heads, 4 levels x
-// 8 points) makes 15 M samples = 61 M corner gathers of 64 bytes and, in the
-// backward, 61 M corner scatters of 128 bytes (fp32). Scattered one by one the
-// backward is bound by the L2 reduction rate (~6 TB/s of RED payload on B200),
-// far above the HBM time of the whole call. But a head-row's samples cluster
-// around one image position across all levels, and head-rows of neighbouring
-// positions hit the same pixels, especially on the coarse levels.
+// 8 points) has 15 M samples. Scattering their 61 M corners one by one into
+// grad_value (fp32, 128 bytes per corner and head) sends 7.6 GB of RED payload
+// to L2, whose reduction rate on B200 (~5-6 TB/s) then bounds the backward far
+// above the HBM time of the whole call. But a head-row's samples cluster
+// around one image position across all levels, and head-rows that sample near
+// each other hit the same pixels, most of all on the coarse levels.
 //
 // Bucketing. Every head-row (b, q, h) gets the key (b, h, tile): tile is the
 // cell of a kTiles x kTiles grid over the normalised image holding the mean of
 // its level-0 sampling locations. A counting sort (count, scan, scatter) lists
-// head-row ids bucket by bucket in `order`; one CTA runs one bucket.
+// head-row ids bucket by bucket in `order` (scratch); one CTA runs one bucket.
 //
-// Staging. A CTA walks its bucket in chunks of up to kMetaCap samples. For each
-// sample one thread computes the geometry once (grid_sample's unnormalisation,
-// corner pixels, bilinear weights times the attention weight) into SampleMeta;
-// lane groups then run the head-rows against the staged samples: corner reads
-// (through L1, which holds the bucket's neighbourhood), unpack, FMA.
+// Scatter. Each level gets a small pixel grid around the bucket's tile. The
+// CTA stages its samples chunk by chunk, sorts the (sample, corner) entries
+// that fall in the grid by pixel (counting sort in shared memory), and lets
+// workers sum each pixel's run of entries in registers: one vector RED per
+// pixel and chunk instead of one per sample corner (about 5x less RED traffic
+// on BEVFormer-like sampling). Corners outside the grid RED directly.
 //
-// Backward scatter. Each level of a bucket gets a small pixel grid around its
-// tile. A chunk's samples whose 2x2 corner footprint lies in the grid are
-// counting-sorted by cell; each grid pixel then sums the contributions of the
-// four cells touching it (weight x grad_out row, in registers) and issues one
-// full-line vector RED. Samples outside the grid scatter their corners
-// directly. The L2 sees one RED per touched pixel per chunk instead of one per
-// sample corner.
+// The backward is then: the row-wise kernel computing grad_loc / grad_w only
+// (msda_backward.cu, full occupancy, no REDs) + this scatter. The forward is
+// the row-wise kernel.
 #include <algorithm>
 
 #include "msda_device.cuh"
@@ -42,15 +37,11 @@ namespace {
 #ifndef MSDA_MARGIN
 #define MSDA_MARGIN 0.03f
 #endif
-#ifndef MSDA_FORWARD_BUCKETED
-#define MSDA_FORWARD_BUCKETED 0
-#endif
 constexpr int kTiles = MSDA_TILES;       // bucket grid per image: kTiles x kTiles
 constexpr float kMargin = MSDA_MARGIN;   // normalised margin of a scatter grid around its tile
 constexpr int kMaxLevels = 16;           // level table entries staged per CTA
 constexpr int kThreads = 256;
-constexpr int kMetaCap = 1024;           // staged samples per chunk
-constexpr int kMaxCells = 2048;          // scatter grid pixels per CTA (all levels)
+constexpr int kMaxCells = 1280;          // scatter grid pixels per CTA (all levels)
 
 struct Rect {    // scatter grid of one level
   int x0, y0;    // level pixel of grid pixel (0, 0)
@@ -58,16 +49,6 @@ struct Rect {    // scatter grid of one level
   int base;      // first grid pixel of the level in the CTA's grid
 };
 
-struct SampleMeta {
-  int4 pix;      // corner pixel (start + y * W + x) in the batch's map, -1 outside the level
-  float4 wa;     // bilinear weight * attention weight per corner
-};
-// Corner order is (y0, x0), (y0, x1), (y1, x0), (y1, x1).
-
-struct SampleAux {  // backward only
-  float lh, lw, a;
-  int slot;         // head-row in the chunk | level << 8 | (grid cell + 1) << 12; cell + 1 == 0: not in the grid
-};
 
 struct BucketPlan {
   int* keys;    // [items]
@@ -206,188 +187,51 @@ __device__ void plan_grids(const Level* levels, Rect* rects, int n_levels, int t
 }
 
 // ---------------------------------------------------------------------------
-// staging
+// grad_value scatter
 // ---------------------------------------------------------------------------
-template <bool kBackward>
-__device__ __forceinline__ void stage_sample(const Level& lv, const Rect* r, float loc_x, float loc_y, float a,
-                                             SampleMeta& m, int& cell, float& lh_out, float& lw_out) {
-  const float fh = static_cast<float>(lv.height), fw = static_cast<float>(lv.width);
-  const float y = unnormalize(loc_y, 0.5f * fh);
-  const float x = unnormalize(loc_x, 0.5f * fw);
-  cell = -1;
-  if (!(y > -2.0f && x > -2.0f && y < fh + 1.0f && x < fw + 1.0f)) {
-    m.pix = make_int4(-1, -1, -1, -1);
-    m.wa = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    lh_out = lw_out = 0.0f;
-    return;
-  }
-  const float yf = floorf(y), xf = floorf(x);
-  const int y0 = static_cast<int>(yf), x0 = static_cast<int>(xf);
-  const float lh = __fsub_rn(y, yf), lw = __fsub_rn(x, xf);
-  const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
-  const bool x0ok = x0 >= 0 && x0 < lv.width, x1ok = x0 + 1 >= 0 && x0 + 1 < lv.width;
-  const bool y0ok = y0 >= 0 && y0 < lv.height, y1ok = y0 + 1 >= 0 && y0 + 1 < lv.height;
-  const int p00 = lv.start + y0 * lv.width + x0;
-  m.pix = make_int4(y0ok && x0ok ? p00 : -1, y0ok && x1ok ? p00 + 1 : -1, y1ok && x0ok ? p00 + lv.width : -1,
-                    y1ok && x1ok ? p00 + lv.width + 1 : -1);
-  m.wa = make_float4(__fmul_rn(hh, hw) * a, __fmul_rn(hh, lw) * a, __fmul_rn(lh, hw) * a, __fmul_rn(lh, lw) * a);
-  lh_out = lh;
-  lw_out = lw;
-  if (kBackward) {
-    const int gx = x0 - r->x0, gy = y0 - r->y0;
-    if (gx >= 0 && gy >= 0 && gx < r->gw - 1 && gy < r->gh - 1) cell = r->base + gy * r->gw + gx;
-  }
-}
+// Per chunk of up to kSampleCap samples of the bucket:
+//   (1) one thread per sample stages its corner weights w_k * a, a validity
+//       mask, and either its grid cell (footprint inside the level's grid) or
+//       the pixel of its corner (y0, x0) (footprint leaves the grid); each
+//       valid corner inside the grid counts one entry for its grid pixel;
+//       the chunk's grad_out rows are copied to shared memory in fp32;
+//   (2) exclusive scan of the per-pixel counts;
+//   (3) one thread per sample places its entries (w_k * a, head-row) at
+//       their pixel's slot: the entries are now sorted by grid pixel;
+//   (4) workers of D/8 lanes take equal slices of the sorted entries; a run of
+//       one pixel is summed in registers (fp32x2 FMAs on 8 channels per lane)
+//       and leaves as two full-sector vector REDs;
+//   (5) corners of samples outside the grid RED directly.
+constexpr int kSampleCap = 1024;  // samples staged per chunk
+constexpr int kItemCap = 64;      // head-rows per chunk
 
-// Stage every sample of head-rows order[first .. first + n); a warp takes
-// whole head-rows (several per pass when they have <= 32 samples).
-template <typename T, bool kBackward>
-__device__ __forceinline__ void stage_chunk(const Dims& d, const Level* levels, const Rect* rects, const T* loc,
-                                            const T* weight, const int* order, int first, int n, SampleMeta* meta,
-                                            SampleAux* aux, int* pix_count, unsigned short* outside,
-                                            int* n_outside) {
-  const int samples = d.levels * d.points;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const int per_pass = samples <= 32 ? 32 / samples : 1;
-  const int lane_item = samples <= 32 ? lane / samples : 0;
-  const int lane_s = samples <= 32 ? lane - lane_item * samples : lane;
-  if (lane_item >= per_pass) return;
-  for (int il = warp * per_pass + lane_item; il < n; il += nwarps * per_pass) {
-    const int64_t item = order[first + il];
-    for (int s = lane_s; s < samples; s += 32) {
-      const int l = s / d.points;
-      const float2 xy = load_loc(loc + (item * samples + s) * 2);
-      const float a = to_f32(weight[item * samples + s]);
-      const int j = il * samples + s;
-      int cell;
-      float lh, lw;
-      stage_sample<kBackward>(levels[l], kBackward ? rects + l : nullptr, xy.x, xy.y, a, meta[j], cell, lh, lw);
-      if (kBackward) {
-        aux[j] = SampleAux{lh, lw, a, il | (l << 8) | ((cell + 1) << 12)};
-        const int4 pix = meta[j].pix;
-        if (cell >= 0) {
-          const int gw = rects[l].gw;
-          if (pix.x >= 0) atomicAdd(pix_count + cell, 1);
-          if (pix.y >= 0) atomicAdd(pix_count + cell + 1, 1);
-          if (pix.z >= 0) atomicAdd(pix_count + cell + gw, 1);
-          if (pix.w >= 0) atomicAdd(pix_count + cell + gw + 1, 1);
-        } else if (pix.x >= 0 || pix.y >= 0 || pix.z >= 0 || pix.w >= 0) {
-          outside[atomicAdd(n_outside, 1)] = static_cast<unsigned short>(j);
-        }
-      }
-    }
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ uint4 corner_row(const T* vlane, int pix, int row_stride) {
-  return pix >= 0 ? ldg16(vlane + static_cast<int64_t>(pix) * row_stride) : make_uint4(0, 0, 0, 0);
-}
-
-// Lane layout shared by both kernels: a group of 2 * LPC lanes per head-row;
-// lane (col, sub) holds 16 bytes (LPC per corner row) of corner column col.
-template <typename T, int LPC>
-struct Layout {
-  static constexpr int kVec = 16 / static_cast<int>(sizeof(T));
-  static constexpr int kD = LPC * kVec;
-  static constexpr int kGroup = 2 * LPC;
-  static constexpr int kGroups = kThreads / kGroup;
-  __host__ __device__ static int items_per_chunk(int samples) {
-    const int cap = kMetaCap / samples;
-    return cap < kGroups * 8 ? cap : kGroups * 8;
-  }
+struct Staged {
+  float4 wa;  // w_k * a for the corners (y0, x0), (y0, x1), (y1, x0), (y1, x1)
+  int where;  // grid cell, or the pixel of corner (y0, x0) when `flags` has kOutside
+  int flags;  // head-row in chunk | level << 8 | corner-valid mask << 12 | kOutside
 };
+constexpr int kOutside = 1 << 16;
 
-// ---------------------------------------------------------------------------
-// forward
-// ---------------------------------------------------------------------------
-template <typename T, int LPC>
-__global__ void __launch_bounds__(kThreads, 3) forward_bucketed_kernel(
-    Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
-    const T* __restrict__ loc, const T* __restrict__ weight, T* __restrict__ out, const int* __restrict__ order,
-    const int* __restrict__ offset) {
-  using L = Layout<T, LPC>;
-  using V = Vec16<T>;
-  constexpr int kVec = L::kVec, kGroup = L::kGroup;
-  __shared__ Level levels[kMaxLevels];
-  __shared__ SampleMeta meta[kMetaCap];
-  const int key = blockIdx.x;
-  const int begin = offset[key], end = offset[key + 1];
-  if (begin == end) return;  // the whole CTA leaves together
-  stage_level_table(d, shapes, starts, levels);
-  __syncthreads();
-  const int bh = key / (kTiles * kTiles), h = bh % d.heads, b = bh / d.heads;
-  const int row_stride = d.heads * d.channels;
-  const int samples = d.levels * d.points;
-  const int lane_g = threadIdx.x % kGroup, col = lane_g / LPC, sub = lane_g % LPC;
-  const T* vlane = value + (static_cast<int64_t>(b) * d.spatial_size) * row_stride + h * d.channels + sub * kVec;
-  const int chunk = L::items_per_chunk(samples);
-  // groups walk the chunk warp by warp: equal trip counts keep the shuffles convergent
-  const int warp_first = (threadIdx.x / 32) * (32 / kGroup), in_warp = (threadIdx.x % 32) / kGroup;
-  for (int first = begin; first < end; first += chunk) {
-    const int n = min(chunk, end - first);
-    stage_chunk<T, false>(d, levels, nullptr, loc, weight, order, first, n, meta, nullptr, nullptr, nullptr, nullptr);
-    __syncthreads();
-    for (int base = warp_first; base < n; base += L::kGroups) {
-      const bool live = base + in_warp < n;
-      const int il = live ? base + in_warp : n - 1;
-      const SampleMeta* m = meta + il * samples;
-      float acc[kVec];
-#pragma unroll
-      for (int i = 0; i < kVec; ++i) acc[i] = 0.0f;
-#pragma unroll 4
-      for (int s = 0; s < samples; ++s) {
-        const int4 pix = m[s].pix;
-        const float4 wa = m[s].wa;
-        float v0[kVec], v1[kVec];
-        V::unpack(corner_row(vlane, col ? pix.y : pix.x, row_stride), v0);
-        V::unpack(corner_row(vlane, col ? pix.w : pix.z, row_stride), v1);
-        const float w0 = col ? wa.y : wa.x, w1 = col ? wa.w : wa.z;
-#pragma unroll
-        for (int i = 0; i < kVec; ++i) acc[i] = fmaf(w1, v1[i], fmaf(w0, v0[i], acc[i]));
-      }
-#pragma unroll
-      for (int i = 0; i < kVec; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], LPC, kGroup);
-      if (live && col == 0) st16(out + static_cast<int64_t>(order[first + il]) * d.channels + sub * kVec, V::pack(acc));
-    }
-    __syncthreads();
-  }
-}
-
-// ---------------------------------------------------------------------------
-// backward
-// ---------------------------------------------------------------------------
-// Per chunk: (1) stage samples, count grid cells, list samples outside the
-// grids; copy the chunk's grad_out rows to shared memory in fp32. (2) lane
-// groups run the head-rows: corner reads and the partial dot products
-// T_k = sum_c g_c v_k,c, from which grad_w = sum_k w_k T_k,
-// grad_x = W a (hh (T_01 - T_00) + lh (T_11 - T_10)),
-// grad_y = H a (hw (T_10 - T_00) + lw (T_11 - T_01)). (3) scan the cell
-// counts and sort the grid samples by cell. (4) every grid pixel sums
-// wa_k * g over the samples of the four cells around it and issues one RED;
-// then the samples outside the grids RED their corners one by one.
-// Scatter workers of the backward: D/8 lanes per worker, 8 fp32 channels
-// each; lane sl owns channels [4 sl, 4 sl + 4) and [D/2 + 4 sl, D/2 + 4 sl + 4),
-// so each of the two REDs of a worker writes D*2 contiguous bytes (whole
-// 32-byte sectors).
+// Scatter workers: D/8 lanes, 8 fp32 channels each; lane sl owns channels
+// [4 sl, 4 sl + 4) and [D/2 + 4 sl, D/2 + 4 sl + 4), so each of a worker's two
+// REDs writes 2D contiguous bytes (whole 32-byte sectors).
 template <int D>
 struct ScatterLayout {
   static constexpr int kLanes = D / 8;
   static constexpr int kWorkers = kThreads / kLanes;
-  __device__ __forceinline__ static void accumulate(const float* grow, int sl, float2 w, float2* acc) {
+  __device__ __forceinline__ static void accumulate(const float* grow, int sl, float w, float2* acc) {
     const float4 a = *reinterpret_cast<const float4*>(grow + 4 * sl);
     const float4 c = *reinterpret_cast<const float4*>(grow + D / 2 + 4 * sl);
-    acc[0] = ffma2(make_float2(a.x, a.y), w, acc[0]);
-    acc[1] = ffma2(make_float2(a.z, a.w), w, acc[1]);
-    acc[2] = ffma2(make_float2(c.x, c.y), w, acc[2]);
-    acc[3] = ffma2(make_float2(c.z, c.w), w, acc[3]);
+    const float2 w2 = make_float2(w, w);
+    acc[0] = ffma2(make_float2(a.x, a.y), w2, acc[0]);
+    acc[1] = ffma2(make_float2(a.z, a.w), w2, acc[1]);
+    acc[2] = ffma2(make_float2(c.x, c.y), w2, acc[2]);
+    acc[3] = ffma2(make_float2(c.z, c.w), w2, acc[3]);
   }
   __device__ __forceinline__ static void red(float* gline, int pixel, int row_stride, int sl, float2* acc) {
-    if (pixel >= 0) {
-      float* dst = gline + static_cast<int64_t>(pixel) * row_stride;
-      red_add_v4(dst + 4 * sl, acc[0].x, acc[0].y, acc[1].x, acc[1].y);
-      red_add_v4(dst + D / 2 + 4 * sl, acc[2].x, acc[2].y, acc[3].x, acc[3].y);
-    }
+    float* dst = gline + static_cast<int64_t>(pixel) * row_stride;
+    red_add_v4(dst + 4 * sl, acc[0].x, acc[0].y, acc[1].x, acc[1].y);
+    red_add_v4(dst + D / 2 + 4 * sl, acc[2].x, acc[2].y, acc[3].x, acc[3].y);
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
   }
@@ -418,63 +262,57 @@ __device__ __forceinline__ void block_exclusive_scan(const int* in, int* out, in
   __syncthreads();
 }
 
-// Shared-memory layout of the backward kernel.
-template <typename T, int LPC>
-struct BackwardSmem {
+template <int D>
+struct ScatterSmem {
   Level* levels;
   Rect* rects;
-  SampleMeta* meta;
-  SampleAux* aux;
-  int* pix_count;    // [kMaxCells]: entries per grid pixel, then the placement cursor
-  int* pix_start;    // [kMaxCells + 1]
-  int* pix_global;   // [kMaxCells]
-  unsigned short* entries;  // [4 kMetaCap]: sample | corner << 10, sorted by grid pixel
-  unsigned short* outside;  // [kMetaCap]: samples whose footprint leaves the grid
-  int* scalars;             // [64]: [0] outside count, [1..32] scan scratch
-  float* gstage;            // [items per chunk][D] grad_out rows in fp32
-  static size_t bytes(int samples) {
-    return 512 + static_cast<size_t>(kMetaCap) * (sizeof(SampleMeta) + sizeof(SampleAux)) +
-           (3 * kMaxCells + 16) * sizeof(int) + 5 * kMetaCap * sizeof(unsigned short) + 64 * sizeof(int) +
-           static_cast<size_t>(Layout<T, LPC>::items_per_chunk(samples)) * Layout<T, LPC>::kD * sizeof(float);
-  }
-  __device__ explicit BackwardSmem(unsigned char* base) {
+  Staged* staged;          // [kSampleCap]
+  float* ent_w;            // [4 kSampleCap]
+  unsigned short* ent_il;  // [4 kSampleCap]
+  unsigned short* outside; // [kSampleCap]
+  int* pix_count;          // [kMaxCells]: entries per grid pixel, then the placement cursor
+  int* pix_start;          // [kMaxCells + 16]
+  int* pix_global;         // [kMaxCells]: pixel of the batch's map, -1 outside the level
+  int* scalars;            // [64]: [0] outside count, [32..63] scan scratch
+  float* gstage;           // [kItemCap][D]
+  static constexpr size_t kBytes = 512 + sizeof(Staged) * kSampleCap + 4 * kSampleCap * (sizeof(float) + 2) +
+                                   2 * kSampleCap + (3 * kMaxCells + 16) * sizeof(int) + 64 * sizeof(int) +
+                                   kItemCap * D * sizeof(float);
+  __device__ explicit ScatterSmem(unsigned char* base) {
     levels = reinterpret_cast<Level*>(base);
     rects = reinterpret_cast<Rect*>(base + sizeof(Level) * kMaxLevels);
-    meta = reinterpret_cast<SampleMeta*>(base + 512);
-    aux = reinterpret_cast<SampleAux*>(meta + kMetaCap);
-    pix_count = reinterpret_cast<int*>(aux + kMetaCap);
+    staged = reinterpret_cast<Staged*>(base + 512);
+    ent_w = reinterpret_cast<float*>(staged + kSampleCap);
+    gstage = ent_w + 4 * kSampleCap;
+    pix_count = reinterpret_cast<int*>(gstage + kItemCap * D);
     pix_start = pix_count + kMaxCells;
     pix_global = pix_start + kMaxCells + 16;
-    entries = reinterpret_cast<unsigned short*>(pix_global + kMaxCells);
-    outside = entries + 4 * kMetaCap;
-    scalars = reinterpret_cast<int*>(outside + kMetaCap);
-    gstage = reinterpret_cast<float*>(scalars + 64);
+    scalars = pix_global + kMaxCells;
+    ent_il = reinterpret_cast<unsigned short*>(scalars + 64);
+    outside = ent_il + 4 * kSampleCap;
   }
 };
 
-template <typename T, int LPC>
-__global__ void __launch_bounds__(kThreads, 2) backward_bucketed_kernel(
-    Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
-    const T* __restrict__ loc, const T* __restrict__ weight, const T* __restrict__ grad_out,
-    float* __restrict__ grad_value, float* __restrict__ grad_loc, float* __restrict__ grad_weight,
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 3) scatter_bucketed_kernel(
+    Dims d, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts, const T* __restrict__ loc,
+    const T* __restrict__ weight, const T* __restrict__ grad_out, float* __restrict__ grad_value,
     const int* __restrict__ order, const int* __restrict__ offset) {
-  using L = Layout<T, LPC>;
+  using S = ScatterLayout<D>;
   using V = Vec16<T>;
-  using S = ScatterLayout<L::kD>;
-  constexpr int kVec = L::kVec, kGroup = L::kGroup, kD = L::kD;
+  constexpr int kVec = V::kLanes;
   extern __shared__ __align__(16) unsigned char smem[];
-  BackwardSmem<T, LPC> sm(smem);
+  ScatterSmem<D> sm(smem);
 
   const int key = blockIdx.x;
   const int begin = offset[key], end = offset[key + 1];
-  if (begin == end) return;
+  if (begin == end) return;  // the whole CTA leaves together
   stage_level_table(d, shapes, starts, sm.levels);
   __syncthreads();
   const int tx = key % kTiles, ty = (key / kTiles) % kTiles, bh = key / (kTiles * kTiles);
   const int h = bh % d.heads, b = bh / d.heads;
   if (threadIdx.x == 0) plan_grids(sm.levels, sm.rects, d.levels, tx, ty);
   __syncthreads();
-  // grid pixel -> pixel of the batch's map (-1 outside the level)
   int cells = 0;
   for (int l = 0; l < d.levels; ++l) {
     const Rect r = sm.rects[l];
@@ -490,146 +328,130 @@ __global__ void __launch_bounds__(kThreads, 2) backward_bucketed_kernel(
 
   const int row_stride = d.heads * d.channels;
   const int samples = d.levels * d.points;
-  const int lane_g = threadIdx.x % kGroup, col = lane_g / LPC, sub = lane_g % LPC;
-  const int64_t head0 = (static_cast<int64_t>(b) * d.spatial_size) * row_stride + h * d.channels;
-  const T* vlane = value + head0 + sub * kVec;
-  const int chunk = L::items_per_chunk(samples);
-  const int warp_first = (threadIdx.x / 32) * (32 / kGroup), in_warp = (threadIdx.x % 32) / kGroup;
-  // scatter workers: S::kLanes lanes per worker, lane sl owns channels [4 sl, 4 sl + 4) and [D/2 + 4 sl, ...)
+  float* gline = grad_value + (static_cast<int64_t>(b) * d.spatial_size) * row_stride + h * d.channels;
   const int worker = threadIdx.x / S::kLanes, sl = threadIdx.x % S::kLanes;
-  float* gline = grad_value + head0;
+  const int chunk = min(kItemCap, kSampleCap / samples);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per_pass = samples <= 32 ? 32 / samples : 1;  // head-rows a warp stages per pass
+  const int lane_item = samples <= 32 ? lane / samples : 0;
+  const int lane_s = samples <= 32 ? lane - lane_item * samples : lane;
 
   for (int first = begin; first < end; first += chunk) {
     const int n = min(chunk, end - first);
     for (int i = threadIdx.x; i < cells; i += blockDim.x) sm.pix_count[i] = 0;
     if (threadIdx.x == 0) sm.scalars[0] = 0;
     __syncthreads();
-    // (1) staging, per-pixel entry counts, and the chunk's grad_out rows in fp32
-    stage_chunk<T, true>(d, sm.levels, sm.rects, loc, weight, order, first, n, sm.meta, sm.aux, sm.pix_count,
-                         sm.outside, sm.scalars);
-    for (int i = threadIdx.x; i < n * LPC; i += blockDim.x) {
-      const int il = i / LPC, part = i % LPC;
+    // (1) staging and per-pixel counts
+    if (lane_item < per_pass) {
+      for (int il = warp * per_pass + lane_item; il < n; il += (kThreads / 32) * per_pass) {
+        const int64_t item = order[first + il];
+        for (int s = lane_s; s < samples; s += 32) {
+          const int l = s / d.points;
+          const Level lv = sm.levels[l];
+          const float2 xy = load_loc(loc + (item * samples + s) * 2);
+          const float a = to_f32(weight[item * samples + s]);
+          const float fh = static_cast<float>(lv.height), fw = static_cast<float>(lv.width);
+          const float y = unnormalize(xy.y, 0.5f * fh);
+          const float x = unnormalize(xy.x, 0.5f * fw);
+          Staged st{make_float4(0.0f, 0.0f, 0.0f, 0.0f), 0, il | (l << 8)};
+          if (y > -2.0f && x > -2.0f && y < fh + 1.0f && x < fw + 1.0f) {
+            const float yf = floorf(y), xf = floorf(x);
+            const int y0 = static_cast<int>(yf), x0 = static_cast<int>(xf);
+            const float lh = __fsub_rn(y, yf), lw = __fsub_rn(x, xf);
+            const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
+            const bool x0ok = x0 >= 0 && x0 < lv.width, x1ok = x0 + 1 < lv.width;
+            const bool y0ok = y0 >= 0 && y0 < lv.height, y1ok = y0 + 1 < lv.height;
+            const int mask = (y0ok && x0ok ? 1 : 0) | (y0ok && x1ok && x0 + 1 >= 0 ? 2 : 0) |
+                             (y1ok && x0ok && y0 + 1 >= 0 ? 4 : 0) | (y1ok && x1ok && x0 + 1 >= 0 && y0 + 1 >= 0 ? 8 : 0);
+            st.wa = make_float4(__fmul_rn(hh, hw) * a, __fmul_rn(hh, lw) * a, __fmul_rn(lh, hw) * a,
+                                __fmul_rn(lh, lw) * a);
+            const Rect r = sm.rects[l];
+            const int gx = x0 - r.x0, gy = y0 - r.y0;
+            if (gx >= 0 && gy >= 0 && gx < r.gw - 1 && gy < r.gh - 1) {
+              st.where = r.base + gy * r.gw + gx;
+              st.flags |= mask << 12;
+              if (mask & 1) atomicAdd(sm.pix_count + st.where, 1);
+              if (mask & 2) atomicAdd(sm.pix_count + st.where + 1, 1);
+              if (mask & 4) atomicAdd(sm.pix_count + st.where + r.gw, 1);
+              if (mask & 8) atomicAdd(sm.pix_count + st.where + r.gw + 1, 1);
+            } else if (mask) {
+              st.where = lv.start + y0 * lv.width + x0;
+              st.flags |= (mask << 12) | kOutside;
+              sm.outside[atomicAdd(sm.scalars, 1)] = static_cast<unsigned short>(il * samples + s);
+            }
+          }
+          sm.staged[il * samples + s] = st;
+        }
+      }
+    }
+    for (int i = threadIdx.x; i < n * (D / kVec); i += blockDim.x) {
+      const int il = i / (D / kVec), part = i % (D / kVec);
       float f[kVec];
       V::unpack(__ldg(reinterpret_cast<const uint4*>(grad_out + static_cast<int64_t>(order[first + il]) * d.channels) +
                       part),
                 f);
 #pragma unroll
       for (int v = 0; v < kVec; v += 4)
-        *reinterpret_cast<float4*>(sm.gstage + il * kD + part * kVec + v) = make_float4(f[v], f[v + 1], f[v + 2], f[v + 3]);
+        *reinterpret_cast<float4*>(sm.gstage + il * D + part * kVec + v) = make_float4(f[v], f[v + 1], f[v + 2], f[v + 3]);
     }
     __syncthreads();
-    // (2) corner reads and the dot products T_k = sum_c g_c v_k,c, one head-row per group
-    for (int base = warp_first; base < n; base += L::kGroups) {
-      const bool live = base + in_warp < n;
-      const int il = live ? base + in_warp : n - 1;
-      const int64_t item = order[first + il];
-      float2 g2[kVec / 2];
-#pragma unroll
-      for (int v = 0; v < kVec; v += 4) {
-        const float4 q = *reinterpret_cast<const float4*>(sm.gstage + il * kD + sub * kVec + v);
-        g2[v / 2] = make_float2(q.x, q.y);
-        g2[v / 2 + 1] = make_float2(q.z, q.w);
-      }
-      const SampleMeta* m = sm.meta + il * samples;
-      const SampleAux* ax = sm.aux + il * samples;
-      int s = 0;
-      for (int l = 0; l < d.levels; ++l) {
-        const float fw = static_cast<float>(sm.levels[l].width), fh = static_cast<float>(sm.levels[l].height);
-#pragma unroll 2
-        for (int p = 0; p < d.points; ++p, ++s) {
-          const int4 pix = m[s].pix;
-          const uint4 r0 = corner_row(vlane, col ? pix.y : pix.x, row_stride);
-          const uint4 r1 = corner_row(vlane, col ? pix.w : pix.z, row_stride);
-          float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
-          const uint32_t w0[4] = {r0.x, r0.y, r0.z, r0.w}, w1[4] = {r1.x, r1.y, r1.z, r1.w};
-#pragma unroll
-          for (int i = 0; i < kVec / 2; ++i) {
-            const float2 v0 = sizeof(T) == 2 ? bf16x2_to_float2(w0[i])
-                                             : make_float2(__uint_as_float(w0[2 * i]), __uint_as_float(w0[2 * i + 1]));
-            const float2 v1 = sizeof(T) == 2 ? bf16x2_to_float2(w1[i])
-                                             : make_float2(__uint_as_float(w1[2 * i]), __uint_as_float(w1[2 * i + 1]));
-            a0 = ffma2(g2[i], v0, a0);
-            a1 = ffma2(g2[i], v1, a1);
-          }
-          float t0 = a0.x + a0.y, t1 = a1.x + a1.y;
-#pragma unroll
-          for (int mask = 1; mask < LPC; mask <<= 1) {
-            t0 += __shfl_xor_sync(0xffffffffu, t0, mask, kGroup);
-            t1 += __shfl_xor_sync(0xffffffffu, t1, mask, kGroup);
-          }
-          const float u0 = __shfl_xor_sync(0xffffffffu, t0, LPC, kGroup);
-          const float u1 = __shfl_xor_sync(0xffffffffu, t1, LPC, kGroup);
-          if (live && lane_g == 0) {  // lane 0 is column 0: T_00 = t0, T_01 = u0, T_10 = t1, T_11 = u1
-            const SampleAux q = ax[s];
-            const float hh = 1.0f - q.lh, hw = 1.0f - q.lw;
-            const int64_t so = item * samples + s;
-            grad_weight[so] = hh * hw * t0 + hh * q.lw * u0 + q.lh * hw * t1 + q.lh * q.lw * u1;
-            *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(
-                fw * q.a * (hh * (u0 - t0) + q.lh * (u1 - t1)), fh * q.a * (hw * (t1 - t0) + q.lw * (u1 - u0)));
-          }
-        }
-      }
-    }
-    // (3) entries (sample, corner) sorted by grid pixel: scan the counts, then place
-    block_exclusive_scan(sm.pix_count, sm.pix_start, cells, sm.scalars + 1);
-    for (int i = threadIdx.x; i < cells; i += blockDim.x) sm.pix_count[i] = sm.pix_start[i];  // placement cursor
+    // (2) pixel offsets
+    block_exclusive_scan(sm.pix_count, sm.pix_start, cells, sm.scalars + 32);
+    for (int i = threadIdx.x; i < cells; i += blockDim.x) sm.pix_count[i] = sm.pix_start[i];
     __syncthreads();
+    // (3) entries sorted by grid pixel
     for (int j = threadIdx.x; j < n * samples; j += blockDim.x) {
-      const int slot = sm.aux[j].slot;
-      const int cell = (slot >> 12) - 1;
-      if (cell < 0) continue;
-      const int gw = sm.rects[(slot >> 8) & 15].gw;
-      const int4 pix = sm.meta[j].pix;
-      const int pk[4] = {pix.x, pix.y, pix.z, pix.w};
+      const Staged st = sm.staged[j];
+      if (st.flags & kOutside) continue;
+      const int mask = (st.flags >> 12) & 15;
+      if (!mask) continue;
+      const int gw = sm.rects[(st.flags >> 8) & 15].gw;
+      const unsigned short il = static_cast<unsigned short>(st.flags & 255);
+      const float w4[4] = {st.wa.x, st.wa.y, st.wa.z, st.wa.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (pk[k] >= 0) sm.entries[atomicAdd(sm.pix_count + cell + (k >> 1) * gw + (k & 1), 1)] =
-                            static_cast<unsigned short>(j | (k << 10));
+      for (int k = 0; k < 4; ++k) {
+        if (!(mask & (1 << k))) continue;
+        const int pos = atomicAdd(sm.pix_count + st.where + (k >> 1) * gw + (k & 1), 1);
+        sm.ent_w[pos] = w4[k];
+        sm.ent_il[pos] = il;
+      }
     }
     __syncthreads();
-    // (4a) equal slices of the pixel-sorted entries: runs of one pixel sum in
-    // registers and leave with one RED
+    // (4) equal slices of the sorted entries; one RED per pixel run
     {
       const int total = sm.pix_start[cells];
       const int per = (total + S::kWorkers - 1) / S::kWorkers;
-      const int e0 = min(total, worker * per), e1 = min(total, e0 + per);
-      if (e0 < e1) {
-        int lo = 0, hi = cells;  // last pixel whose start <= e0
+      int e = min(total, worker * per);
+      const int e1 = min(total, e + per);
+      if (e < e1) {
+        int lo = 0, hi = cells;  // the pixel whose range holds e: last start <= e
         while (hi - lo > 1) {
           const int mid = (lo + hi) >> 1;
-          if (sm.pix_start[mid] <= e0) lo = mid; else hi = mid;
+          if (sm.pix_start[mid] <= e) lo = mid; else hi = mid;
         }
-        int pixel = lo, next = sm.pix_start[pixel + 1];
-        bool pending = false;
+        int pixel = lo;
         float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
                          make_float2(0.0f, 0.0f)};
-        for (int e = e0; e < e1; ++e) {
-          while (e >= next) {  // the run of `pixel` ended; empty pixels in between send nothing
-            if (pending) S::red(gline, sm.pix_global[pixel], row_stride, sl, acc);
-            pending = false;
-            ++pixel;
-            next = sm.pix_start[pixel + 1];
-          }
-          const int ent = sm.entries[e];
-          const int j = ent & 1023, k = ent >> 10;
-          const float w = reinterpret_cast<const float*>(&sm.meta[j].wa)[k];
-          S::accumulate(sm.gstage + (sm.aux[j].slot & 255) * kD, sl, make_float2(w, w), acc);
-          pending = true;
+        while (e < e1) {
+          const int stop = min(e1, sm.pix_start[pixel + 1]);
+#pragma unroll 4
+          for (; e < stop; ++e) S::accumulate(sm.gstage + sm.ent_il[e] * D, sl, sm.ent_w[e], acc);
+          S::red(gline, sm.pix_global[pixel], row_stride, sl, acc);
+          while (e < e1 && e >= sm.pix_start[pixel + 1]) ++pixel;  // skip to the next non-empty pixel
         }
-        if (pending) S::red(gline, sm.pix_global[pixel], row_stride, sl, acc);
       }
     }
-    // (4b) samples outside the grids: every in-level corner directly
+    // (5) corners of samples outside the grid
     const int n_out = sm.scalars[0];
-    for (int e = worker; e < n_out * 4; e += S::kWorkers) {
-      const int j = sm.outside[e >> 2], k = e & 3;
-      const int pix = reinterpret_cast<const int*>(&sm.meta[j].pix)[k];
-      if (pix < 0) continue;
-      const float w = reinterpret_cast<const float*>(&sm.meta[j].wa)[k];
+    for (int t = worker; t < n_out * 4; t += S::kWorkers) {
+      const Staged st = sm.staged[sm.outside[t >> 2]];
+      const int k = t & 3;
+      if (!((st.flags >> 12) & (1 << k))) continue;
+      const int width = sm.levels[(st.flags >> 8) & 15].width;
       float2 acc[4] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f),
                        make_float2(0.0f, 0.0f)};
-      S::accumulate(sm.gstage + (sm.aux[j].slot & 255) * kD, sl, make_float2(w, w), acc);
-      S::red(gline, pix, row_stride, sl, acc);
+      S::accumulate(sm.gstage + (st.flags & 255) * D, sl, reinterpret_cast<const float*>(&st.wa)[k], acc);
+      S::red(gline, st.where + (k >> 1) * width + (k & 1), row_stride, sl, acc);
     }
     __syncthreads();
   }
@@ -638,18 +460,18 @@ __global__ void __launch_bounds__(kThreads, 2) backward_bucketed_kernel(
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-// Lanes per corner row for the bucketed kernels, or 0 when they do not apply.
-int bucketed_lanes(const Dims& d, size_t elem, const Args& a) {
-  const int g = vec_group(d.channels, elem, a);
-  if (g != 2 && g != 4 && g != 8 && g != 16) return 0;
-  if (d.channels % 4 != 0 || d.channels / 4 > 2 * g) return 0;  // one fp32 line within a group
-  if (d.levels < 1 || d.levels > kMaxLevels) return 0;
+// Whether the bucketed grad_value scatter applies (else the row-wise backward
+// scatters its own corners).
+bool scatter_applies(DType dtype, const Dims& d, const Args& a) {
+  const size_t elem = dtype == DType::kBF16 ? 2 : 4;
+  if (vec_group(d.channels, elem, a) == 0) return false;  // the row-wise dot kernel must be the vector one
+  if (d.channels != 16 && d.channels != 32 && d.channels != 64 && d.channels != 128) return false;
+  if (d.levels < 1 || d.levels > kMaxLevels) return false;
   const int samples = d.levels * d.points;
-  if (samples < 1 || samples > kMetaCap) return 0;
+  if (samples < 1 || samples > kSampleCap) return false;
   const int64_t buckets = static_cast<int64_t>(d.batch) * d.heads * kTiles * kTiles;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
-  if (buckets >= (1LL << 30) || items >= (1LL << 31) - 1) return 0;
-  return g;
+  return buckets < (1LL << 30) && items < (1LL << 31) - 1;
 }
 
 size_t plan_bytes(const Dims& d) {
@@ -684,87 +506,82 @@ cudaError_t bucketize(const Dims& d, const Args& a, const BucketPlan& plan, cuda
   return cudaGetLastError();
 }
 
-
-template <typename T, int LPC>
-cudaError_t launch_bucketed(bool forward, const Dims& d, const Args& a, const BucketPlan& plan, cudaStream_t stream) {
-  if (forward) {
-    forward_bucketed_kernel<T, LPC><<<plan.buckets, kThreads, 0, stream>>>(
-        d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
-        static_cast<const T*>(a.weight), static_cast<T*>(a.out), plan.order, plan.offset);
-    return cudaGetLastError();
-  }
-  const size_t smem = BackwardSmem<T, LPC>::bytes(d.levels * d.points);
-  auto kernel = backward_bucketed_kernel<T, LPC>;
+template <typename T, int D>
+cudaError_t launch_scatter(const Dims& d, const Args& a, const BucketPlan& plan, cudaStream_t stream) {
+  auto kernel = scatter_bucketed_kernel<T, D>;
+  constexpr size_t smem = ScatterSmem<D>::kBytes;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  kernel<<<plan.buckets, kThreads, smem, stream>>>(
-      d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
-      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight,
-      plan.order, plan.offset);
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);  // room for 3 CTAs
+  if (err != cudaSuccess) return err;
+  kernel<<<plan.buckets, kThreads, smem, stream>>>(d, a.shapes, a.starts, static_cast<const T*>(a.loc),
+                                                    static_cast<const T*>(a.weight),
+                                                    static_cast<const T*>(a.grad_out), a.grad_value, plan.order,
+                                                    plan.offset);
   return cudaGetLastError();
 }
 
+// Backward = row-wise dot products (grad_loc, grad_w) + bucketed grad_value scatter.
 template <typename T>
-cudaError_t run_bucketed(bool forward, const Dims& d, const Args& a, int lpc, const BucketPlan& plan,
-                         cudaStream_t stream) {
-  cudaError_t err = bucketize<T>(d, a, plan, stream);
+cudaError_t split_backward(DType dtype, const Dims& d, const Args& a, const BucketPlan& plan, cudaStream_t stream) {
+  Args dots = a;
+  dots.skip_grad_value = true;
+  cudaError_t err = launch_backward_rowwise(dtype, d, dots, stream);
   if (err != cudaSuccess) return err;
-  switch (lpc) {
-    case 2: return launch_bucketed<T, 2>(forward, d, a, plan, stream);
-    case 4: return launch_bucketed<T, 4>(forward, d, a, plan, stream);
-    case 8: return launch_bucketed<T, 8>(forward, d, a, plan, stream);
-    default: return launch_bucketed<T, 16>(forward, d, a, plan, stream);
+  err = bucketize<T>(d, a, plan, stream);
+  if (err != cudaSuccess) return err;
+  switch (d.channels) {
+    case 16: return launch_scatter<T, 16>(d, a, plan, stream);
+    case 32: return launch_scatter<T, 32>(d, a, plan, stream);
+    case 64: return launch_scatter<T, 64>(d, a, plan, stream);
+    default: return launch_scatter<T, 128>(d, a, plan, stream);
   }
 }
 
-// Scratch comes from the stream-ordered allocator (cudaMallocAsync) and goes
-// back to it right after the launches; a failed allocation falls back to the
-// row-wise kernels, which need no scratch.
-cudaError_t dispatch(bool forward, DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
-  const size_t elem = dtype == DType::kBF16 ? 2 : 4;
-#if MSDA_FORWARD_BUCKETED
-  const int lpc = bucketed_lanes(d, elem, a);
-#else
-  const int lpc = forward ? 0 : bucketed_lanes(d, elem, a);
-#endif
-  if (lpc != 0) {
-    void* scratch = nullptr;
-    if (cudaMallocAsync(&scratch, plan_bytes(d), stream) == cudaSuccess) {
-      const BucketPlan plan = carve(scratch, d);
-      cudaError_t err = dtype == DType::kBF16 ? run_bucketed<__nv_bfloat16>(forward, d, a, lpc, plan, stream)
-                                              : run_bucketed<float>(forward, d, a, lpc, plan, stream);
-      const cudaError_t ferr = cudaFreeAsync(scratch, stream);
-      return err != cudaSuccess ? err : ferr;
-    }
-    (void)cudaGetLastError();  // clear the allocation failure
-  }
-  return forward ? launch_forward_rowwise(dtype, d, a, stream) : launch_backward_rowwise(dtype, d, a, stream);
+cudaError_t backward_with_plan(DType dtype, const Dims& d, const Args& a, void* scratch, cudaStream_t stream) {
+  const BucketPlan plan = carve(scratch, d);
+  return dtype == DType::kBF16 ? split_backward<__nv_bfloat16>(dtype, d, a, plan, stream)
+                               : split_backward<float>(dtype, d, a, plan, stream);
 }
 
 }  // namespace
 
 cudaError_t launch_forward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
   if (d.batch == 0 || d.queries == 0 || d.heads == 0 || d.channels == 0) return cudaSuccess;
-  return dispatch(true, dtype, d, a, stream);
+  return launch_forward_rowwise(dtype, d, a, stream);
 }
 
+#ifndef MSDA_BUCKETED_BACKWARD
+#define MSDA_BUCKETED_BACKWARD 0
+#endif
+
+// The fused row-wise backward (gathers, dot products and corner REDs in one
+// pass) measures faster than dot products + bucketed scatter on every
+// configuration so far, so it is the default. MSDA_BUCKETED_BACKWARD=1 builds
+// the split form, with its bucket plan from the stream-ordered allocator.
 cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {
   if (d.batch == 0 || d.queries == 0 || d.heads == 0) return cudaSuccess;
-  return dispatch(false, dtype, d, a, stream);
+  if (MSDA_BUCKETED_BACKWARD && scatter_applies(dtype, d, a)) {
+    void* scratch = nullptr;
+    if (cudaMallocAsync(&scratch, plan_bytes(d), stream) == cudaSuccess) {
+      const cudaError_t err = backward_with_plan(dtype, d, a, scratch, stream);
+      const cudaError_t ferr = cudaFreeAsync(scratch, stream);
+      return err != cudaSuccess ? err : ferr;
+    }
+    (void)cudaGetLastError();  // clear the allocation failure
+  }
+  return launch_backward_rowwise(dtype, d, a, stream);
 }
 
 size_t backward_scratch_bytes(DType dtype, const Dims& d, const Args& a) {
   if (d.batch == 0 || d.queries == 0 || d.heads == 0) return 0;
-  return bucketed_lanes(d, dtype == DType::kBF16 ? 2 : 4, a) != 0 ? plan_bytes(d) : 0;
+  return scatter_applies(dtype, d, a) ? plan_bytes(d) : 0;
 }
 
 cudaError_t launch_backward_on_scratch(DType dtype, const Dims& d, const Args& a, void* scratch, cudaStream_t stream) {
   if (d.batch == 0 || d.queries == 0 || d.heads == 0) return cudaSuccess;
-  const int lpc = bucketed_lanes(d, dtype == DType::kBF16 ? 2 : 4, a);
-  if (lpc == 0) return launch_backward_rowwise(dtype, d, a, stream);
-  const BucketPlan plan = carve(scratch, d);
-  return dtype == DType::kBF16 ? run_bucketed<__nv_bfloat16>(false, d, a, lpc, plan, stream)
-                               : run_bucketed<float>(false, d, a, lpc, plan, stream);
+  if (!scatter_applies(dtype, d, a)) return launch_backward_rowwise(dtype, d, a, stream);
+  return backward_with_plan(dtype, d, a, scratch, stream);
 }
 
 }  // namespace msda

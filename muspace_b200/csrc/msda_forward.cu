@@ -47,10 +47,9 @@ __global__ void __launch_bounds__(256) forward_vec_kernel(Dims d, const T* __res
     const T* lp = loc + item * samples * 2;
     const T* wp = weight + item * samples;
 
-    // channel pairs accumulate with packed fp32x2 FMAs: acc += (w_k a) v_k
-    float2 acc[kVec / 2];
+    float acc[kVec];
 #pragma unroll
-    for (int i = 0; i < kVec / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < kVec; ++i) acc[i] = 0.0f;
 
     for (int l = 0; l < d.levels; ++l) {
       const Level lv = levels[l];
@@ -65,27 +64,17 @@ __global__ void __launch_bounds__(256) forward_vec_kernel(Dims d, const T* __res
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           raw[k] = c.row[k] >= 0 ? ldg16(vbase + static_cast<int64_t>(c.row[k]) * row_stride) : make_uint4(0, 0, 0, 0);
+        float v[4][kVec];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float wk = c.w[k] * a;
-          const float2 w2 = make_float2(wk, wk);
-          const uint32_t words[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+        for (int k = 0; k < 4; ++k) V::unpack(raw[k], v[k]);
 #pragma unroll
-          for (int i = 0; i < kVec / 2; ++i) {
-            const float2 v2 = sizeof(T) == 2 ? bf16x2_to_float2(words[i])
-                                             : make_float2(__uint_as_float(words[2 * i]), __uint_as_float(words[2 * i + 1]));
-            acc[i] = ffma2(v2, w2, acc[i]);
-          }
+        for (int i = 0; i < kVec; ++i) {
+          const float bil = c.w[0] * v[0][i] + c.w[1] * v[1][i] + c.w[2] * v[2][i] + c.w[3] * v[3][i];
+          acc[i] = fmaf(bil, a, acc[i]);
         }
       }
     }
-    float flat[kVec];
-#pragma unroll
-    for (int i = 0; i < kVec / 2; ++i) {
-      flat[2 * i] = acc[i].x;
-      flat[2 * i + 1] = acc[i].y;
-    }
-    st16(out + item * d.channels + sub * kVec, V::pack(flat));
+    st16(out + item * d.channels + sub * kVec, V::pack(acc));
   }
 }
 

@@ -31,6 +31,7 @@ struct Args {
   float* grad_loc;
   float* grad_weight;
   const int* order;  // optional head-row visiting order (row-wise kernels); null = natural
+  bool skip_grad_value;  // row-wise backward: grad_loc / grad_w only (grad_value comes from elsewhere)
 };
 
 // Grid-stride kernels never need more CTAs than this; 148 SMs x 8 resident
