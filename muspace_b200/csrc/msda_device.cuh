@@ -85,6 +85,53 @@ struct Vec16<__nv_bfloat16> {
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
+// ---------------------------------------------------------------------------
+// lane slices: kBytes of one head-row's channels per lane
+// ---------------------------------------------------------------------------
+// A head-row of D channels is split over G = D * sizeof(T) / kBytes lanes.
+// Slice<T, kBytes> loads a lane's bytes and widens them to fp32 channel pairs
+// (kPairs float2; channel 2i in .x, 2i+1 in .y).
+template <int kWords>
+struct Words {
+  uint32_t w[kWords];
+};
+
+template <int kBytes>
+__device__ __forceinline__ Words<kBytes / 4> ldg_words(const void* p) {
+  Words<kBytes / 4> r;
+  if constexpr (kBytes == 16) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    r.w[0] = v.x, r.w[1] = v.y, r.w[2] = v.z, r.w[3] = v.w;
+  } else {
+    static_assert(kBytes == 8, "lane slices are 8 or 16 bytes");
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    r.w[0] = v.x, r.w[1] = v.y;
+  }
+  return r;
+}
+
+template <typename T, int kBytes>
+struct Slice {
+  static constexpr int kChannels = kBytes / static_cast<int>(sizeof(T));
+  static constexpr int kPairs = kChannels / 2;
+  __device__ __forceinline__ static float2 pair(const Words<kBytes / 4>& r, int i) {
+    if constexpr (sizeof(T) == 2) {
+      return make_float2(__uint_as_float(r.w[i] << 16), __uint_as_float(r.w[i] & 0xffff0000u));
+    } else {
+      return make_float2(__uint_as_float(r.w[2 * i]), __uint_as_float(r.w[2 * i + 1]));
+    }
+  }
+};
+
+// Zero-filled words for a corner outside the level.
+template <int kWords>
+__device__ __forceinline__ Words<kWords> zero_words() {
+  Words<kWords> r;
+#pragma unroll
+  for (int i = 0; i < kWords; ++i) r.w[i] = 0u;
+  return r;
+}
+
 // Streaming read of data used exactly once (locations, weights, grad_out):
 // do not keep it in L1, and let L2 evict it first so the value maps stay.
 __device__ __forceinline__ uint64_t evict_first_policy() {
@@ -98,6 +145,27 @@ __device__ __forceinline__ uint4 ld_stream16(const void* p, uint64_t policy) {
   asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p), "l"(policy));
+  return r;
+}
+
+__device__ __forceinline__ uint2 ld_stream8(const void* p, uint64_t policy) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p), "l"(policy));
+  return r;
+}
+
+template <int kBytes>
+__device__ __forceinline__ Words<kBytes / 4> ld_stream_words(const void* p, uint64_t policy) {
+  Words<kBytes / 4> r;
+  if constexpr (kBytes == 16) {
+    const uint4 v = ld_stream16(p, policy);
+    r.w[0] = v.x, r.w[1] = v.y, r.w[2] = v.z, r.w[3] = v.w;
+  } else {
+    const uint2 v = ld_stream8(p, policy);
+    r.w[0] = v.x, r.w[1] = v.y;
+  }
   return r;
 }
 
@@ -194,6 +262,50 @@ __device__ __forceinline__ bool corners(const Level& lv, float loc_x, float loc_
 }
 
 // ---------------------------------------------------------------------------
+// staged sample geometry (row-wise vector kernels)
+// ---------------------------------------------------------------------------
+// Threads per CTA of the row-wise vector kernels (their shared staging arrays
+// have one slot per thread).
+constexpr int kCtaThreads = 256;
+
+// The G lanes of a group take the samples of a head-row in chunks of
+// kSamples = min(G, kMax); the lane at sub = i * kStagerStride computes the
+// geometry of sample i of the chunk for the whole group.
+template <int G, int kMax>
+struct Chunk {
+  static constexpr int kSamples = G < kMax ? G : kMax;
+  static constexpr int kStagerStride = G / kSamples;
+};
+
+// Computes sample s of a head-row (locations lp, weights wp) and stores its
+// four corner rows (-1 = outside the level, or no sample) and w_k * a in the
+// caller's shared slots. Returns the sample's (lh, lw, a) and whether it has a
+// corner inside its level, for the gradient formulas.
+template <typename T>
+__device__ __forceinline__ bool stage_sample(const Level* levels, int points, int samples, bool live, int s,
+                                             const T* lp, const T* wp, int4* row_slot, float4* wa_slot,
+                                             float4* geo = nullptr) {
+  int4 r = make_int4(-1, -1, -1, -1);
+  float4 wa = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  bool valid = false;
+  if (live && s < samples) {
+    const Level lv = levels[s / points];
+    const float2 xy = load_loc(lp + 2 * s);
+    const float a = to_f32(wp[s]);
+    Corners c;
+    valid = corners(lv, xy.x, xy.y, c);
+    if (valid) {
+      r = make_int4(c.row[0], c.row[1], c.row[2], c.row[3]);
+      wa = make_float4(c.w[0] * a, c.w[1] * a, c.w[2] * a, c.w[3] * a);
+      if (geo) *geo = make_float4(c.lh, c.lw, a, 0.0f);
+    }
+  }
+  *row_slot = r;
+  *wa_slot = wa;
+  return valid;
+}
+
+// ---------------------------------------------------------------------------
 // lane-group reductions and gradient scatter
 // ---------------------------------------------------------------------------
 // Sum over the G lanes of a group (G a power of two <= 32, groups aligned).
@@ -241,5 +353,55 @@ struct RedSlice<__nv_bfloat16, G> {
     red_add_v4(head_row + 4 * G + 4 * sub, wa * gr[4], wa * gr[5], wa * gr[6], wa * gr[7]);
   }
 };
+
+// t[C][4] holds a lane's partial corner dots for the C samples of a chunk.
+// Sums them over the G lanes of the group so that every lane with
+// sub / (G / C) == i ends with sample i's totals in t[0]: first log2(C)
+// halving exchanges over the high lane bits (a lane keeps half of the samples
+// it holds and sends the other half to its xor partner, 4 values each), then
+// plain butterflies over the remaining low bits.
+template <int G, int C, int M = G / 2, int N = C>
+__device__ __forceinline__ void reduce_to_stagers(float (&t)[C][4], int sub) {
+  if constexpr (M >= 1) {
+    if constexpr (N > 1) {
+      const bool upper = (sub & M) != 0;
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float send = upper ? t[i][k] : t[i + N / 2][k];
+          const float keep = upper ? t[i + N / 2][k] : t[i][k];
+          t[i][k] = keep + __shfl_xor_sync(0xffffffffu, send, M);
+        }
+      }
+      reduce_to_stagers<G, C, M / 2, N / 2>(t, sub);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) t[0][k] += __shfl_xor_sync(0xffffffffu, t[0][k], M);
+      reduce_to_stagers<G, C, M / 2, 1>(t, sub);
+    }
+  }
+}
+
+// Two fp32 products in one instruction (sm_100 mul.rn.f32x2).
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  F2 x, y, r;
+  x.f = a;
+  y.f = b;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.u) : "l"(x.u), "l"(y.u));
+  return r.f;
+}
+
+// grad_value[corner row] += wa * g over a lane's own channel slice
+// (kPairs * 2 fp32 channels, 16-byte aligned): one vector RED per 4 channels.
+template <int kPairs>
+__device__ __forceinline__ void scatter_slice(float* dst, float wa, const float2 (&g2)[kPairs]) {
+  const float2 w2 = make_float2(wa, wa);
+#pragma unroll
+  for (int q = 0; q < kPairs / 2; ++q) {
+    const float2 lo = fmul2(w2, g2[2 * q]), hi = fmul2(w2, g2[2 * q + 1]);
+    red_add_v4(dst + 4 * q, lo.x, lo.y, hi.x, hi.y);
+  }
+}
 
 }  // namespace msda

@@ -11,70 +11,102 @@
 // of G = D * sizeof(T) / 16 lanes owns it and each lane holds 16 bytes of
 // channels (8 bf16 or 4 fp32). For D = 32 that is 4 lanes (bf16) or 8 lanes
 // (fp32), so a warp runs 8 or 4 head-rows at once and every corner gather is
-// one 16-byte load per lane, 64 / 128 contiguous bytes per group. Locations
-// and weights are read by the group's lanes together (one broadcast
-// transaction) and the point loop is unrolled so several samples' corner
-// loads are in flight per thread. Items are ordered batch-major, so at any
-// moment the CTAs in flight gather from one or two cameras' value maps, which
-// stay resident in L2. Any other D takes the scalar kernel below.
+// one 16-byte load per lane, 64 / 128 contiguous bytes per group.
+//
+// The sample geometry (level, unnormalised coordinate, the four corner rows
+// and bilinear weights) is the same for every lane of a group, so it is not
+// computed G times: the samples are taken in chunks of C = min(G, 8), the
+// lane at sub = i * G / C computes sample i of the chunk and stages its four
+// corner rows and w_k * a in shared memory, and the whole group then reads
+// them back (one broadcast load each) while it gathers. Items are ordered
+// batch-major, so at any moment the CTAs in flight gather from one or two
+// cameras' value maps, which stay resident in L2. Any other D takes the
+// scalar kernel below.
 #include "msda_device.cuh"
 
 namespace msda {
 
+#ifndef MSDA_FWD_PACKED
+#define MSDA_FWD_PACKED 1
+#endif
+
 template <typename T, int G>
-__global__ void __launch_bounds__(256) forward_vec_kernel(Dims d, const T* __restrict__ value,
-                                                          const int64_t* __restrict__ shapes,
-                                                          const int64_t* __restrict__ starts,
-                                                          const T* __restrict__ loc, const T* __restrict__ weight,
-                                                          T* __restrict__ out, const int* __restrict__ order) {
-  using V = Vec16<T>;
-  constexpr int kVec = V::kLanes;
+__global__ void __launch_bounds__(kCtaThreads) forward_vec_kernel(Dims d, const T* __restrict__ value,
+                                                               const int64_t* __restrict__ shapes,
+                                                               const int64_t* __restrict__ starts,
+                                                               const T* __restrict__ loc, const T* __restrict__ weight,
+                                                               T* __restrict__ out, const int* __restrict__ order) {
+  using S = Slice<T, 16>;
+  constexpr int kCh = S::kChannels, kPairs = S::kPairs, kWords = 4;
+  constexpr int C = Chunk<G, 8>::kSamples, kOwn = Chunk<G, 8>::kStagerStride;
   extern __shared__ Level levels[];
+  __shared__ int4 s_row[kCtaThreads];
+  __shared__ float4 s_wa[kCtaThreads];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
-  const int groups_per_cta = blockDim.x / G;
+  const int base = threadIdx.x - sub;
+  const bool stager = sub % kOwn == 0;
+  const int mine = sub / kOwn;
+  constexpr int kGroups = kCtaThreads / G;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int row_stride = d.heads * d.channels;  // elements between neighbouring pixels
   const int samples = d.levels * d.points;
 
-  for (int64_t slot = static_cast<int64_t>(blockIdx.x) * groups_per_cta + threadIdx.x / G; slot < items;
-       slot += static_cast<int64_t>(gridDim.x) * groups_per_cta) {
-    const int64_t item = order ? order[slot] : slot;
+  // Whole warps take the same number of trips (the trip count depends only on
+  // the warp's first item), so the warp-wide syncs below are convergent.
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
+  for (int64_t slot = static_cast<int64_t>(blockIdx.x) * kGroups + threadIdx.x / G;
+       slot - (threadIdx.x % 32) / G < items; slot += stride) {
+    const bool live = slot < items;
+    const int64_t item = order ? order[live ? slot : items - 1] : (live ? slot : items - 1);
     const int h = static_cast<int>(item % d.heads);
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
-    const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kVec;
+    const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     const T* lp = loc + item * samples * 2;
     const T* wp = weight + item * samples;
 
-    float acc[kVec];
+    float2 acc[kPairs];
 #pragma unroll
-    for (int i = 0; i < kVec; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kPairs; ++i) acc[i] = make_float2(0.0f, 0.0f);
 
-    for (int l = 0; l < d.levels; ++l) {
-      const Level lv = levels[l];
-#pragma unroll 4
-      for (int p = 0; p < d.points; ++p) {
-        const int s = l * d.points + p;
-        const float2 xy = load_loc(lp + 2 * s);
-        const float a = to_f32(wp[s]);
-        Corners c;
-        if (!corners(lv, xy.x, xy.y, c)) continue;
-        uint4 raw[4];
+    for (int s0 = 0; s0 < samples; s0 += C) {
+      if (stager) stage_sample(levels, d.points, samples, live, s0 + mine, lp, wp, s_row + threadIdx.x, s_wa + threadIdx.x);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < C; ++i) {
+        const int4 r4 = s_row[base + i * kOwn];
+        const float4 w4 = s_wa[base + i * kOwn];
+        const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+        const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+        Words<kWords> raw[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          raw[k] = c.row[k] >= 0 ? ldg16(vbase + static_cast<int64_t>(c.row[k]) * row_stride) : make_uint4(0, 0, 0, 0);
-        float v[4][kVec];
+          raw[k] = rows[k] >= 0 ? ldg_words<16>(vbase + static_cast<int64_t>(rows[k]) * row_stride) : zero_words<kWords>();
 #pragma unroll
-        for (int k = 0; k < 4; ++k) V::unpack(raw[k], v[k]);
+        for (int k = 0; k < 4; ++k) {
+#if MSDA_FWD_PACKED
+          const float2 w2 = make_float2(wa[k], wa[k]);
 #pragma unroll
-        for (int i = 0; i < kVec; ++i) {
-          const float bil = c.w[0] * v[0][i] + c.w[1] * v[1][i] + c.w[2] * v[2][i] + c.w[3] * v[3][i];
-          acc[i] = fmaf(bil, a, acc[i]);
+          for (int q = 0; q < kPairs; ++q) acc[q] = ffma2(w2, S::pair(raw[k], q), acc[q]);
+#else
+#pragma unroll
+          for (int q = 0; q < kPairs; ++q) {
+            const float2 v = S::pair(raw[k], q);
+            acc[q].x = fmaf(wa[k], v.x, acc[q].x);
+            acc[q].y = fmaf(wa[k], v.y, acc[q].y);
+          }
+#endif
         }
       }
+      __syncwarp();
     }
-    st16(out + item * d.channels + sub * kVec, V::pack(acc));
+    if (live) {
+      float f[kCh];
+#pragma unroll
+      for (int q = 0; q < kPairs; ++q) f[2 * q] = acc[q].x, f[2 * q + 1] = acc[q].y;
+      st16(out + item * d.channels + sub * kCh, Vec16<T>::pack(f));
+    }
   }
 }
 
@@ -121,12 +153,11 @@ __global__ void __launch_bounds__(256) forward_scalar_kernel(Dims d, const T* __
 
 template <typename T, int G>
 static cudaError_t launch_forward_vec(const Dims& d, const Args& a, cudaStream_t stream) {
-  constexpr int kThreads = 256;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
-  const int64_t groups_per_cta = kThreads / G;
+  const int64_t groups_per_cta = kCtaThreads / G;
   const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
-  forward_vec_kernel<T, G><<<grid, kThreads, level_smem(d), stream>>>(
+  forward_vec_kernel<T, G><<<grid, kCtaThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<T*>(a.out), a.order);
   return cudaGetLastError();
@@ -144,11 +175,10 @@ static cudaError_t launch_forward_t(const Dims& d, const Args& a, cudaStream_t s
     case 32: return launch_forward_vec<T, 32>(d, a, stream);
     default: break;
   }
-  constexpr int kThreads = 256;
   const int64_t total = static_cast<int64_t>(d.batch) * d.queries * d.heads * d.channels;
-  const int64_t blocks = (total + kThreads - 1) / kThreads;
+  const int64_t blocks = (total + kCtaThreads - 1) / kCtaThreads;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
-  forward_scalar_kernel<T><<<grid, kThreads, level_smem(d), stream>>>(
+  forward_scalar_kernel<T><<<grid, kCtaThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<T*>(a.out));
   return cudaGetLastError();

@@ -34,29 +34,42 @@ struct Args {
   bool skip_grad_value;  // row-wise backward: grad_loc / grad_w only (grad_value comes from elsewhere)
 };
 
-// Grid-stride kernels never need more CTAs than this; 148 SMs x 8 resident
-// 256-thread CTAs x 16 waves keeps every SM busy without a tail of idle CTAs.
-inline int64_t grid_cap() { return 148LL * 8 * 16; }
+// Most CTAs a launch asks for; beyond it the kernels' grid-stride loops take
+// over. Items are meant to be visited roughly in order (batch-major) so the
+// CTAs in flight share one camera's value map and grad_value lines in L2; a
+// small cap makes each CTA stride across many cameras and spreads the working
+// set beyond L2, so the cap only guards gridDim.x.
+#ifndef MSDA_GRID_CAP
+#define MSDA_GRID_CAP (1LL << 30)
+#endif
+inline int64_t grid_cap() { return MSDA_GRID_CAP; }
 
 inline size_t level_smem(const Dims& d) { return sizeof(Level) * static_cast<size_t>(d.levels > 0 ? d.levels : 1); }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Lanes per head-row for the 16-byte vector kernels, or 0 when the channel
-// count / alignment needs the scalar kernels.
-inline int vec_group(int channels, size_t elem, const Args& a) {
+// Lanes per head-row when each lane holds lane_bytes (8 or 16) of channels,
+// or 0 when the channel count / alignment rules that layout out: G must be a
+// power of two up to a warp, the channel slices must be aligned to lane_bytes
+// and the fp32 gradient slices to 16 bytes.
+inline int vec_lanes(int channels, size_t elem, size_t lane_bytes, const Args& a) {
   const size_t row_bytes = static_cast<size_t>(channels) * elem;
-  if (row_bytes == 0 || row_bytes % 16 != 0) return 0;
-  const size_t g = row_bytes / 16;
+  if (row_bytes == 0 || row_bytes % lane_bytes != 0) return 0;
+  const size_t g = row_bytes / lane_bytes;
   if (g != 1 && g != 2 && g != 4 && g != 8 && g != 16 && g != 32) return 0;
-  if (!aligned16(a.value)) return 0;
+  if (lane_bytes / elem < 4) return 0;  // a lane's fp32 gradient slice must fill whole 16-byte REDs
+  const auto aligned = [lane_bytes](const void* p) { return (reinterpret_cast<uintptr_t>(p) % lane_bytes) == 0; };
+  if (!aligned(a.value)) return 0;
   if ((reinterpret_cast<uintptr_t>(a.loc) % (2 * elem)) != 0) return 0;  // (x, y) pairs load as one word
-  if (a.out && !aligned16(a.out)) return 0;
-  if (a.grad_out && !aligned16(a.grad_out)) return 0;
+  if (a.out && !aligned(a.out)) return 0;
+  if (a.grad_out && !aligned(a.grad_out)) return 0;
   if (a.grad_value && !aligned16(a.grad_value)) return 0;
   if ((reinterpret_cast<uintptr_t>(a.grad_loc) & 7u) != 0) return 0;  // (x, y) gradients store as one float2
   return static_cast<int>(g);
 }
+
+// Lanes per head-row for the 16-byte vector kernels (forward, bucketed scatter).
+inline int vec_group(int channels, size_t elem, const Args& a) { return vec_lanes(channels, elem, 16, a); }
 
 // Entry points used by the C-ABI: pick the tiled path when it applies and
 // fall back to the row-wise kernels otherwise (msda_tiled.cu).

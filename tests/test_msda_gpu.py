@@ -116,6 +116,48 @@ def test_c_abi_matches_c_oracle(cuda_device, name):
         _close(gw, exp_gw, FP32_TOL, f"{name}/{dtype}:grad_w")
 
 
+def _random_case(channels, levels, points, seed, batch=2, queries=7, heads=2):
+    """Seeded inputs with locations spread over [-0.1, 1.1] (some corners and
+    samples outside their level)."""
+    rng = np.random.default_rng(seed)
+    shapes = np.array([(5, 7), (3, 4), (2, 2), (1, 3)][:levels], dtype=np.int64)
+    start = np.concatenate([[0], np.cumsum(shapes[:, 0] * shapes[:, 1])[:-1]]).astype(np.int64)
+    lin = int((shapes[:, 0] * shapes[:, 1]).sum())
+    f = np.float32
+    return {
+        "value": rng.standard_normal((batch, lin, heads, channels)).astype(f),
+        "spatial_shapes": shapes,
+        "level_start_index": start,
+        "sampling_locations": rng.uniform(-0.1, 1.1, (batch, queries, heads, levels, points, 2)).astype(f),
+        "attention_weights": rng.uniform(0, 1, (batch, queries, heads, levels, points)).astype(f),
+        "grad_output": rng.standard_normal((batch, queries, heads * channels)).astype(f),
+    }
+
+
+@pytest.mark.parametrize("channels", [4, 8, 128, 256])
+@pytest.mark.parametrize("levels,points", [(3, 3), (1, 1), (4, 2)])
+def test_every_lane_layout_matches_c_oracle(cuda_device, channels, levels, points):
+    """Head-rows of 4..256 channels take every lane layout of the vector
+    kernels (1 to 32 lanes of 8 or 16 bytes, and the scalar kernels for fp32
+    D = 256); 1, 8 and 9 samples per head-row cover a chunk of staged samples
+    that is partly empty, exactly full, or followed by a short one."""
+    g = _random_case(channels, levels, points, seed=channels * 100 + levels * 10 + points)
+    for dtype, tol in ((torch.float32, FP32_TOL), (torch.bfloat16, BF16_TOL)):
+        q = {k: (torch.from_numpy(v).to(dtype).float().numpy() if v.dtype == np.float32 else v) for k, v in g.items()}
+        args = [q[k] for k in INPUTS]
+        exp_out = oracle_forward(*args)
+        exp_gv, exp_gl, exp_gw = oracle_backward(*args, q["grad_output"])
+        inp = {k: torch.from_numpy(v).to(cuda_device) for k, v in q.items()}
+        inp = {k: (v.to(dtype) if v.dtype.is_floating_point else v) for k, v in inp.items()}
+        out, (gv, gl, gw) = _c_abi_fwd_bwd(inp, dtype)
+        torch.cuda.synchronize()
+        what = f"D={channels} L={levels} P={points} {dtype}"
+        _close(out, exp_out, tol, f"{what}:output")
+        _close(gv, exp_gv, FP32_TOL, f"{what}:grad_value")
+        _close(gl, exp_gl, FP32_TOL, f"{what}:grad_loc")
+        _close(gw, exp_gw, FP32_TOL, f"{what}:grad_w")
+
+
 def test_bf16_keeps_sampling_geometry_in_fp32(cuda_device):
     """Reference test 430-468: pixels 499 | 500 hold 0 | 4096, x = 499.5 -> 2048."""
     width = 1000
