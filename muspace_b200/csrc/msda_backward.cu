@@ -18,18 +18,24 @@
 // B200 design. A group of G lanes owns a head-row; each lane holds kBytes of
 // its channels (bf16: 8 bytes = 4 channels, fp32: 16 bytes = 4 channels, so
 // bf16 D = 32 runs 8 lanes and one RED instruction of the group covers the
-// corner's whole 128-byte fp32 grad_value line). Samples are taken in chunks
-// of C = min(G, 4) (2 for fp32): the lane at sub = i * G / C computes the geometry of
-// chunk sample i once and stages its corner rows and w_k * a in shared
-// memory. Every lane then, per sample, gathers its slice of the four corners,
-// forms the corner dots T_k = sum_c g_c v_k,c over its channels (packed fp32x2
-// FMAs) and scatters w_k * a * g with red.global.add.v4.f32 (no return value).
-// A transpose reduction hands each staging lane the four T_k of its own sample,
-// from which it writes
-//   grad_w = sum_k w_k T_k,
-//   grad_x = W a (hh (T_1 - T_0) + lh (T_3 - T_2)),
-//   grad_y = H a (hw (T_2 - T_0) + lw (T_3 - T_1)),
-// so the C staging lanes of a group store C consecutive samples' gradients.
+// corner's whole 128-byte fp32 grad_value line). The head-row's samples are
+// taken in chunks of Cs = min(G, 8) (4 for head-rows of at most 4 samples):
+//  1. stage: the lane at sub = i * G / Cs computes the geometry of chunk
+//     sample i once and stages its four corner rows, w_k * a and (lh, lw, a)
+//     in shared memory;
+//  2. fold: the chunk's 4 Cs (corner row, w_k * a) entries are merged by row
+//     (samples of one head-row cluster, so at coarse levels most corners
+//     repeat: on BEVFormer-like locations 117 corner rows per head-row shrink
+//     to 72); a repeated row's w_k * a moves to its first occurrence;
+//  3. per sample: every lane gathers its slice of the four corners, forms the
+//     corner dots T_k = sum_c g_c v_k,c over its channels (packed fp32x2
+//     FMAs) and sends (sum of w_k * a) * g for each first-occurrence row with
+//     red.global.add.v4.f32; after every round of Cd samples (4 for bf16, 2
+//     for fp32) a transpose reduction hands one lane per sample the four T_k,
+//     from which it writes
+//       grad_w = sum_k w_k T_k,
+//       grad_x = W a (hh (T_1 - T_0) + lh (T_3 - T_2)),
+//       grad_y = H a (hw (T_2 - T_0) + lw (T_3 - T_1)).
 #include "msda_device.cuh"
 
 namespace msda {
@@ -40,40 +46,97 @@ namespace msda {
 #ifndef MSDA_BWD_MINBLOCKS_F32
 #define MSDA_BWD_MINBLOCKS_F32 3
 #endif
-// Samples staged per chunk (the partial dots of a chunk live in registers:
-// 4 per sample) and CTAs per SM the register budget is sized for; measured
-// on B200 (fp32 D = 32: chunk 2 at 3 CTAs/SM beats chunk 4 at 2 or 3).
+#ifndef MSDA_BWD_MINBLOCKS_BF16
+#define MSDA_BWD_MINBLOCKS_BF16 3
+#endif
+#ifndef MSDA_BWD_DEDUP
+#define MSDA_BWD_DEDUP 1
+#endif
+// Samples per dot round (their partial dots live in registers: 4 per sample)
+// and CTAs per SM the register budget is sized for; measured on B200 (fp32
+// D = 32: rounds of 2 at 3 CTAs/SM beat rounds of 4 at 2 or 3).
 template <typename T>
 constexpr int kChunk = sizeof(T) == 2 ? 4 : MSDA_BWD_CHUNK_F32;
 template <typename T, int kBytes>
-constexpr int kMinBlocks = sizeof(T) == 2 ? (kBytes == 8 ? 3 : 2) : MSDA_BWD_MINBLOCKS_F32;
+constexpr int kMinBlocks = sizeof(T) == 2 ? (kBytes == 8 ? MSDA_BWD_MINBLOCKS_BF16 : 2) : MSDA_BWD_MINBLOCKS_F32;
+
+// Folds repeated corner rows of a chunk's kEnt staged (row, wa) entries into
+// their first occurrence: an entry whose row already appears at a lower
+// index adds its wa to that entry (shared-memory atomic) and its own wa
+// becomes 0, so a RED is due exactly for the entries with row >= 0 and
+// wa != 0. Rows are left as they are (the gathers still need them). Lane sub
+// of the group owns entries sub, sub + G, ...
+template <int G, int kEnt>
+__device__ __forceinline__ void fold_repeated_rows(const int* row, float* wa, int sub) {
+  static_assert(kEnt % 4 == 0, "entries come in whole samples");
+  constexpr int kPer = (kEnt + G - 1) / G;
+  int mine[kPer], target[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = sub + j * G;
+    mine[j] = e < kEnt ? row[e] : -1;
+    target[j] = -1;
+  }
+  // earliest lower-index entry with the same row; only entries below
+  // (j + 1) * G can precede entry j, so the scan stops there
+#pragma unroll
+  for (int e4 = 0; e4 < ((kPer - 1) * G + G < kEnt ? (kPer - 1) * G + G : kEnt); e4 += 4) {
+    const int4 r4 = *reinterpret_cast<const int4*>(row + e4);
+    const int rs[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e2 = e4 + u;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        if (e2 >= (j + 1) * G) continue;  // never below entry j
+        const bool before = e2 < j * G || e2 < sub + j * G;
+        if (before && target[j] < 0 && rs[u] == mine[j] && mine[j] >= 0) target[j] = e2;
+      }
+    }
+  }
+  float moved[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = sub + j * G;
+    moved[j] = (target[j] >= 0) ? wa[e] : 0.0f;
+  }
+  __syncwarp();  // every lane has read the wa it moves before any entry changes
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (target[j] >= 0) {
+      atomicAdd(wa + target[j], moved[j]);
+      wa[sub + j * G] = 0.0f;
+    }
+  }
+  __syncwarp();
+}
 
 // kScatter = false computes grad_loc / grad_w only; grad_value then comes from
 // the bucketed scatter kernel (msda_bucketed.cu).
-template <typename T, int G, int kBytes, bool kScatter>
-__global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_vec_kernel(Dims d, const T* __restrict__ value,
-                                                                      const int64_t* __restrict__ shapes,
-                                                                      const int64_t* __restrict__ starts,
-                                                                      const T* __restrict__ loc,
-                                                                      const T* __restrict__ weight,
-                                                                      const T* __restrict__ grad_out,
-                                                                      float* __restrict__ grad_value,
-                                                                      float* __restrict__ grad_loc,
-                                                                      float* __restrict__ grad_weight,
-                                                                      const int* __restrict__ order) {
+template <typename T, int G, int kBytes, int kStageMax, bool kScatter>
+__global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_vec_kernel(
+    Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
+    const T* __restrict__ loc, const T* __restrict__ weight, const T* __restrict__ grad_out,
+    float* __restrict__ grad_value, float* __restrict__ grad_loc, float* __restrict__ grad_weight,
+    const int* __restrict__ order) {
   using S = Slice<T, kBytes>;
   constexpr int kCh = S::kChannels, kPairs = S::kPairs, kWords = kBytes / 4;
-  constexpr int C = Chunk<G, kChunk<T>>::kSamples, kOwn = Chunk<G, kChunk<T>>::kStagerStride;
+  constexpr int Cs = G < kStageMax ? G : kStageMax;       // samples staged per chunk
+  constexpr int kStage = G / Cs;                           // stager lanes: sub % kStage == 0
+  constexpr int Cd = Cs < kChunk<T> ? Cs : kChunk<T>;      // samples per dot round
+  constexpr int kFin = G / Cd;                             // finishing lanes: sub % kFin == 0
   constexpr int kGroups = kCtaThreads / G;
+  // Each group's Cs slots plus one of padding, so the groups of a warp reading
+  // their slot i at once hit different shared-memory banks.
+  constexpr int kSlots = Cs + 1;
   extern __shared__ Level levels[];
-  __shared__ int4 s_row[kCtaThreads];
-  __shared__ float4 s_wa[kCtaThreads];
+  __shared__ int4 s_row[kGroups * kSlots];
+  __shared__ float4 s_wa[kGroups * kSlots];
+  __shared__ float4 s_geo[kGroups * kSlots];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
-  const int base = threadIdx.x - sub;
-  const bool stager = sub % kOwn == 0;
-  const int mine = sub / kOwn;
+  const int base = (threadIdx.x / G) * kSlots;  // the group's slots are base .. base + Cs - 1
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int row_stride = d.heads * d.channels;
   const int samples = d.levels * d.points;
@@ -102,56 +165,73 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
       for (int q = 0; q < kPairs; ++q) g2[q] = S::pair(graw, q);
     }
 
-    for (int s0 = 0; s0 < samples; s0 += C) {
-      float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      bool valid = false;
-      if (stager) valid = stage_sample(levels, d.points, samples, live, s0 + mine, lp, wp, s_row + threadIdx.x,
-                                       s_wa + threadIdx.x, &geo);
+    for (int s0 = 0; s0 < samples; s0 += Cs) {
+      // 1. stage
+      if (sub % kStage == 0) {
+        const int i = sub / kStage;
+        float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo);
+        s_geo[base + i] = geo;
+      }
       __syncwarp();
-      float t[C][4];
+#if MSDA_BWD_DEDUP
+      // 2. one RED per distinct corner row of the chunk
+      if constexpr (kScatter)
+        fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(s_row + base),
+                                      reinterpret_cast<float*>(s_wa + base), sub);
+#endif
+      // 3. per sample: gathers, corner dots, the sample's REDs; per round the
+      // gradients of the locations / weights
 #pragma unroll
-      for (int i = 0; i < C; ++i) {
-        const int4 r4 = s_row[base + i * kOwn];
-        const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
-        Words<kWords> raw[4];
+      for (int r = 0; r < Cs / Cd; ++r) {
+        float t[Cd][4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          raw[k] = rows[k] >= 0 ? ldg_words<kBytes>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
-                                : zero_words<kWords>();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float2 acc = make_float2(0.0f, 0.0f);
-#pragma unroll
-          for (int q = 0; q < kPairs; ++q) acc = ffma2(g2[q], S::pair(raw[k], q), acc);
-          t[i][k] = acc.x + acc.y;
-        }
-        if constexpr (kScatter) {
-          const float4 w4 = s_wa[base + i * kOwn];
-          const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+        for (int i = 0; i < Cd; ++i) {
+          const int4 r4 = s_row[base + r * Cd + i];
+          const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+          Words<kWords> raw[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            if (rows[k] >= 0) scatter_slice<kPairs>(gbase + static_cast<int64_t>(rows[k]) * row_stride, wa[k], g2);
+            raw[k] = rows[k] >= 0 ? ldg_words<kBytes>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
+                                  : zero_words<kWords>();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < kPairs; ++q) acc = ffma2(g2[q], S::pair(raw[k], q), acc);
+            t[i][k] = acc.x + acc.y;
+          }
+          if constexpr (kScatter) {
+            const float4 w4 = s_wa[base + r * Cd + i];
+            const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (rows[k] >= 0 && wa[k] != 0.0f)
+                scatter_slice<kPairs>(gbase + static_cast<int64_t>(rows[k]) * row_stride, wa[k], g2);
+          }
+        }
+        reduce_to_stagers<G, Cd>(t, sub);
+        const int i = sub / kFin;
+        const int s = s0 + r * Cd + i;
+        if (sub % kFin == 0 && live && s < samples) {
+          const float4 geo = s_geo[base + r * Cd + i];
+          float gw = 0.0f, gx = 0.0f, gy = 0.0f;
+          if (geo.w != 0.0f) {
+            const Level lv = levels[s / d.points];
+            const float lh = geo.x, lw = geo.y, a = geo.z;
+            const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
+            const float* tt = t[0];
+            gw = __fmul_rn(hh, hw) * tt[0] + __fmul_rn(hh, lw) * tt[1] + __fmul_rn(lh, hw) * tt[2] +
+                 __fmul_rn(lh, lw) * tt[3];
+            gx = static_cast<float>(lv.width) * a * (hh * (tt[1] - tt[0]) + lh * (tt[3] - tt[2]));
+            gy = static_cast<float>(lv.height) * a * (hw * (tt[2] - tt[0]) + lw * (tt[3] - tt[1]));
+          }
+          const int64_t so = it * samples + s;
+          grad_weight[so] = gw;
+          *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(gx, gy);
         }
       }
       __syncwarp();  // the next chunk's staging overwrites the slots read above
-      reduce_to_stagers<G, C>(t, sub);
-      const int s = s0 + mine;
-      if (stager && live && s < samples) {
-        float gw = 0.0f, gx = 0.0f, gy = 0.0f;
-        if (valid) {
-          const Level lv = levels[s / d.points];
-          const float lh = geo.x, lw = geo.y, a = geo.z;
-          const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
-          const float* tt = t[0];
-          gw = __fmul_rn(hh, hw) * tt[0] + __fmul_rn(hh, lw) * tt[1] + __fmul_rn(lh, hw) * tt[2] +
-               __fmul_rn(lh, lw) * tt[3];
-          gx = static_cast<float>(lv.width) * a * (hh * (tt[1] - tt[0]) + lh * (tt[3] - tt[2]));
-          gy = static_cast<float>(lv.height) * a * (hw * (tt[2] - tt[0]) + lw * (tt[3] - tt[1]));
-        }
-        const int64_t so = it * samples + s;
-        grad_weight[so] = gw;
-        *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(gx, gy);
-      }
     }
   }
 }
@@ -218,7 +298,12 @@ static cudaError_t launch_backward_vec(const Dims& d, const Args& a, cudaStream_
   const int64_t groups_per_cta = kCtaThreads / G;
   const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
-  auto kernel = a.skip_grad_value ? backward_vec_kernel<T, G, kBytes, false> : backward_vec_kernel<T, G, kBytes, true>;
+  // head-rows of at most 4 samples (single-level cases) stage 4 at a time
+  const bool short_rows = d.levels * d.points <= 4;
+  auto kernel = short_rows ? (a.skip_grad_value ? backward_vec_kernel<T, G, kBytes, 4, false>
+                                                : backward_vec_kernel<T, G, kBytes, 4, true>)
+                           : (a.skip_grad_value ? backward_vec_kernel<T, G, kBytes, 8, false>
+                                                : backward_vec_kernel<T, G, kBytes, 8, true>);
   kernel<<<grid, kCtaThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight,

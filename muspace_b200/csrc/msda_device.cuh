@@ -279,8 +279,9 @@ struct Chunk {
 
 // Computes sample s of a head-row (locations lp, weights wp) and stores its
 // four corner rows (-1 = outside the level, or no sample) and w_k * a in the
-// caller's shared slots. Returns the sample's (lh, lw, a) and whether it has a
-// corner inside its level, for the gradient formulas.
+// caller's shared slots. Returns whether the sample has a corner inside its
+// level, and, when geo is given, stores (lh, lw, a, 1) there for a valid
+// sample (the caller zeroes it), for the gradient formulas.
 template <typename T>
 __device__ __forceinline__ bool stage_sample(const Level* levels, int points, int samples, bool live, int s,
                                              const T* lp, const T* wp, int4* row_slot, float4* wa_slot,
@@ -297,7 +298,7 @@ __device__ __forceinline__ bool stage_sample(const Level* levels, int points, in
     if (valid) {
       r = make_int4(c.row[0], c.row[1], c.row[2], c.row[3]);
       wa = make_float4(c.w[0] * a, c.w[1] * a, c.w[2] * a, c.w[3] * a);
-      if (geo) *geo = make_float4(c.lh, c.lw, a, 0.0f);
+      if (geo) *geo = make_float4(c.lh, c.lw, a, 1.0f);
     }
   }
   *row_slot = r;
