@@ -186,6 +186,55 @@ MSDA_API int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t 
                                           const void *grad_output, float *grad_value, float *grad_sampling_loc,
                                           float *grad_attn_weight, void *stream);
 
+/*
+ * BEVFormer spatial cross-attention, forward fused with the rebatch scatter
+ * and the camera-count normalisation, for ONE camera:
+ *
+ *   for b < B, q < valid_len, h < Hh:
+ *     slots[b, index[q], h, :] += MSDA(b * cams + cam_id, q, h) / count[b, index[q]]
+ *
+ * Replaces ms_deformable_im2col_scatter_div_musa,
+ * csrc/ms_deformable_attn/ms_deform_attn_musa.mu:455-505 (kernel
+ * ms_deform_attn_musa_kernel.muh:419-486), which the reference compiled but
+ * never exported; its argument list (batch_size, num_cams, cam_id,
+ * valid_len, max_len, num_query, ...) is read here from the views:
+ *   value               (B * cams, Lin, Hh, D)       storage dtype
+ *   sampling_locations  (B * cams, max_len, Hh, L, P, 2), attention_weights
+ *                       (B * cams, max_len, Hh, L, P): the rebatched queries
+ *   index               (valid_len,) int64, valid_len <= max_len: the BEV
+ *                       query of each of this camera's first valid_len rows;
+ *                       distinct entries (a BEV query appears once per camera)
+ *   count               (B, num_query) storage dtype: cameras per BEV query
+ *   slots               (B, num_query, Hh * D) storage dtype, updated in place
+ * The update is a read-modify-write in the storage dtype (as in the
+ * reference), race-free because index holds distinct queries; call the
+ * cameras one after another (one stream) to accumulate all of them. An index
+ * entry outside [0, num_query) updates nothing. The MSDA term is the same
+ * sampling as ms_deform_attn_forward (grid_sample convention). Needs D *
+ * element size a multiple of 16 bytes up to 512 (D = 32 in BEVFormer).
+ */
+MSDA_API int ms_deform_attn_scatter_div_forward(const DLTensor *value, const DLTensor *spatial_shapes,
+                                               const DLTensor *level_start_index, const DLTensor *sampling_locations,
+                                               const DLTensor *attention_weights, const DLTensor *index,
+                                               const DLTensor *count, DLTensor *slots, int cam_id, void *stream);
+
+/* Sizes of the rebatch side of the fused scatter (plain-pointer form). */
+typedef struct {
+  int64_t batch;     /* B: batch entries (count / slots dim 0) */
+  int64_t cams;      /* cameras per batch entry; dims->batch = batch * cams */
+  int64_t cam;       /* the camera of this call */
+  int64_t valid_len; /* rows of this camera that carry a BEV query (index length) */
+  int64_t num_query; /* BEV queries (count / slots dim 1) */
+} msda_slot_dims_t;
+
+/* Plain-pointer form of ms_deform_attn_scatter_div_forward; dims describes the
+ * rebatched MSDA call (batch = B * cams, queries = max_len). */
+MSDA_API int msda_scatter_div_forward(msda_dtype_t dtype, const msda_dims_t *dims, const msda_slot_dims_t *slot_dims,
+                                      const void *value, const int64_t *spatial_shapes,
+                                      const int64_t *level_start_index, const void *sampling_locations,
+                                      const void *attention_weights, const int64_t *index, const void *count,
+                                      void *slots, void *stream);
+
 /* Message of the last failed call on this thread ("" after a success). The
  * reference raised it as a TVM-FFI exception (csrc/ffi/tensor_utils.hpp:13-34). */
 MSDA_API const char *msda_last_error(void);

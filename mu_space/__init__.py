@@ -17,6 +17,7 @@ from muspace_b200 import __all__, __version__  # noqa: F401
 _SUBMODULES = (
     "ops",
     "ops.multi_scale_deformable_attn",
+    "ops.sca_scatter",
     "runtime",
     "runtime.kernel_dispatch",
     "runtime.native",

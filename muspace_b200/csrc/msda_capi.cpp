@@ -61,8 +61,12 @@ void check_tensor(const DLTensor* t, const char* name, uint8_t code, uint8_t bit
                                                 dtype_name(t->dtype));
   require(t->ndim == ndim, std::string(name) + " must have " + std::to_string(ndim) + " dims, got " +
                                std::to_string(t->ndim));
-  for (int i = 0; i < ndim; ++i) require(t->shape[i] >= 0, std::string(name) + " has a negative extent");
-  if (t->strides != nullptr) {
+  bool empty = false;
+  for (int i = 0; i < ndim; ++i) {
+    require(t->shape[i] >= 0, std::string(name) + " has a negative extent");
+    empty = empty || t->shape[i] == 0;
+  }
+  if (t->strides != nullptr && !empty) {  // a view without elements has no layout to check
     int64_t expect = 1;
     for (int i = ndim - 1; i >= 0; --i) {
       if (t->shape[i] != 1)
@@ -324,6 +328,96 @@ int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t* dims, co
     if (need > 0) check_launch(msda::static_scratch_address(&scratch), "static scratch set-up");
     check_launch(msda::launch_backward_on_scratch(dt, kd, a, scratch, static_cast<cudaStream_t>(stream)),
                  "msda_backward_static_scratch");
+  });
+}
+
+int ms_deform_attn_scatter_div_forward(const DLTensor* value, const DLTensor* spatial_shapes,
+                                      const DLTensor* level_start_index, const DLTensor* sampling_locations,
+                                      const DLTensor* attention_weights, const DLTensor* index, const DLTensor* count,
+                                      DLTensor* slots, int cam_id, void* stream) {
+  return guarded([&] {
+    const msda::DType dt = storage_dtype(value);
+    const uint8_t code = dt == msda::DType::kBF16 ? kDLBfloat : kDLFloat;
+    const uint8_t bits = dt == msda::DType::kBF16 ? 16 : 32;
+    const int dev = value->device.device_id;
+    check_tensor(value, "value", code, bits, 4, dev);
+    check_tensor(spatial_shapes, "spatial_shapes", kDLInt, 64, 2, dev);
+    check_tensor(level_start_index, "level_start_index", kDLInt, 64, 1, dev);
+    check_tensor(sampling_locations, "sampling_locations", code, bits, 6, dev);
+    check_tensor(attention_weights, "attention_weights", code, bits, 5, dev);
+    check_tensor(index, "index", kDLInt, 64, 1, dev);
+    check_tensor(count, "count", code, bits, 2, dev);
+    check_tensor(slots, "slots", code, bits, 3, dev);
+    // the rebatched call: B * cams images, max_len query slots per image
+    const msda_dims_t d =
+        dims_from_views(value, spatial_shapes, level_start_index, sampling_locations, attention_weights, 1 << 30);
+    msda_slot_dims_t sd{};
+    sd.batch = count->shape[0];
+    sd.num_query = count->shape[1];
+    sd.valid_len = index->shape[0];
+    sd.cam = cam_id;
+    require(sd.batch > 0 && d.batch % sd.batch == 0,
+            "value batch (" + std::to_string(d.batch) + ") must be count batch (" + std::to_string(sd.batch) +
+                ") times the number of cameras");
+    sd.cams = d.batch / sd.batch;
+    require(cam_id >= 0 && cam_id < sd.cams,
+            "cam_id " + std::to_string(cam_id) + " outside [0, " + std::to_string(sd.cams) + ")");
+    require(sd.valid_len <= d.queries, "index is longer than the rebatched query dimension (max_len)");
+    require(slots->shape[0] == sd.batch && slots->shape[1] == sd.num_query && slots->shape[2] == d.heads * d.channels,
+            "slots must have shape (B, num_query, Hh * D)");
+    require(sd.num_query <= std::numeric_limits<int32_t>::max(), "num_query exceeds 2^31");
+    DeviceGuard guard(dev);
+    msda::Args a{};
+    a.value = data_of(value);
+    a.shapes = static_cast<const int64_t*>(data_of(spatial_shapes));
+    a.starts = static_cast<const int64_t*>(data_of(level_start_index));
+    a.loc = data_of(sampling_locations);
+    a.weight = data_of(attention_weights);
+    const msda::SlotDims ks{static_cast<int>(sd.batch), static_cast<int>(sd.cams), static_cast<int>(sd.cam),
+                            static_cast<int>(sd.valid_len), static_cast<int>(sd.num_query)};
+    const cudaError_t err = msda::launch_scatter_div(dt, to_kernel_dims(d), ks, a,
+                                                     static_cast<const int64_t*>(data_of(index)), data_of(count),
+                                                     data_of(slots), static_cast<cudaStream_t>(stream));
+    require(err != cudaErrorInvalidValue,
+            "ms_deform_attn_scatter_div_forward needs Hh * D rows in 16-byte lane slices (D * element size a "
+            "multiple of 16 up to 512 bytes) and 16-byte aligned tensors");
+    check_launch(err, "ms_deform_attn_scatter_div_forward");
+  });
+}
+
+int msda_scatter_div_forward(msda_dtype_t dtype, const msda_dims_t* dims, const msda_slot_dims_t* slot_dims,
+                             const void* value, const int64_t* spatial_shapes, const int64_t* level_start_index,
+                             const void* sampling_locations, const void* attention_weights, const int64_t* index,
+                             const void* count, void* slots, void* stream) {
+  return guarded([&] {
+    require(dtype == MSDA_DTYPE_FLOAT32 || dtype == MSDA_DTYPE_BFLOAT16, "dtype must be float32 or bfloat16");
+    require(dims != nullptr && slot_dims != nullptr, "dims is null");
+    check_dims(*dims);
+    const msda_slot_dims_t& sd = *slot_dims;
+    const int64_t kMax = std::numeric_limits<int32_t>::max();
+    require(sd.batch >= 0 && sd.cams > 0 && sd.valid_len >= 0 && sd.num_query >= 0 && sd.num_query <= kMax,
+            "slot sizes must be non-negative (cams positive, num_query < 2^31)");
+    require(dims->batch == sd.batch * sd.cams, "dims->batch must be slot_dims->batch * slot_dims->cams");
+    require(sd.cam >= 0 && sd.cam < sd.cams, "cam outside [0, cams)");
+    require(sd.valid_len <= dims->queries, "valid_len exceeds the rebatched query dimension (dims->queries)");
+    const bool empty = sd.batch * sd.valid_len * dims->heads * dims->channels == 0;
+    require(empty || (value && spatial_shapes && level_start_index && sampling_locations && attention_weights &&
+                      index && count && slots),
+            "a required pointer is null");
+    msda::Args a{};
+    a.value = value;
+    a.shapes = spatial_shapes;
+    a.starts = level_start_index;
+    a.loc = sampling_locations;
+    a.weight = attention_weights;
+    const msda::DType dt = dtype == MSDA_DTYPE_BFLOAT16 ? msda::DType::kBF16 : msda::DType::kF32;
+    const msda::SlotDims ks{static_cast<int>(sd.batch), static_cast<int>(sd.cams), static_cast<int>(sd.cam),
+                            static_cast<int>(sd.valid_len), static_cast<int>(sd.num_query)};
+    const cudaError_t err =
+        msda::launch_scatter_div(dt, to_kernel_dims(*dims), ks, a, index, count, slots, static_cast<cudaStream_t>(stream));
+    require(err != cudaErrorInvalidValue,
+            "msda_scatter_div_forward needs Hh * D rows in 16-byte lane slices and 16-byte aligned pointers");
+    check_launch(err, "msda_scatter_div_forward");
   });
 }
 

@@ -30,6 +30,68 @@ namespace msda {
 #define MSDA_FWD_PACKED 1
 #endif
 
+// Staging slots of the forward kernels: C = min(G, 8) samples per chunk plus
+// one slot of padding per group, so the groups of a warp reading slot i at
+// once hit different shared-memory banks.
+template <int G>
+struct FwdSlots {
+  static constexpr int kSamples = Chunk<G, 8>::kSamples;
+  static constexpr int kStride = Chunk<G, 8>::kStagerStride;
+  static constexpr int kPerGroup = kSamples + 1;
+  static constexpr int kTotal = (kCtaThreads / G) * kPerGroup;
+};
+
+// acc (this lane's channel pairs) += sum over the head-row's samples of
+// sum_k (w_k a) v_k. vbase points at the lane's channel slice of pixel 0 of
+// the head's value map; lp / wp at the head-row's locations / weights; row /
+// wa at the group's staging slots. Every lane of the warp must call it (it
+// syncs the warp), live = false for a lane group without an item.
+template <typename T, int G>
+__device__ __forceinline__ void gather_head_row(const Level* levels, int points, int samples, bool live,
+                                                const T* vbase, int row_stride, const T* lp, const T* wp, int sub,
+                                                int4* row, float4* wa, float2 (&acc)[Slice<T, 16>::kPairs]) {
+  using S = Slice<T, 16>;
+  constexpr int kPairs = S::kPairs, kWords = 4;
+  constexpr int C = FwdSlots<G>::kSamples, kOwn = FwdSlots<G>::kStride;
+#pragma unroll
+  for (int i = 0; i < kPairs; ++i) acc[i] = make_float2(0.0f, 0.0f);
+  for (int s0 = 0; s0 < samples; s0 += C) {
+    if (sub % kOwn == 0) {
+      const int i = sub / kOwn;
+      stage_sample(levels, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int4 r4 = row[i];
+      const float4 w4 = wa[i];
+      const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+      const float was[4] = {w4.x, w4.y, w4.z, w4.w};
+      Words<kWords> raw[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        raw[k] = rows[k] >= 0 ? ldg_words<16>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
+                              : zero_words<kWords>();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+#if MSDA_FWD_PACKED
+        const float2 w2 = make_float2(was[k], was[k]);
+#pragma unroll
+        for (int q = 0; q < kPairs; ++q) acc[q] = ffma2(w2, S::pair(raw[k], q), acc[q]);
+#else
+#pragma unroll
+        for (int q = 0; q < kPairs; ++q) {
+          const float2 v = S::pair(raw[k], q);
+          acc[q].x = fmaf(was[k], v.x, acc[q].x);
+          acc[q].y = fmaf(was[k], v.y, acc[q].y);
+        }
+#endif
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <typename T, int G>
 __global__ void __launch_bounds__(kCtaThreads) forward_vec_kernel(Dims d, const T* __restrict__ value,
                                                                const int64_t* __restrict__ shapes,
@@ -37,24 +99,21 @@ __global__ void __launch_bounds__(kCtaThreads) forward_vec_kernel(Dims d, const 
                                                                const T* __restrict__ loc, const T* __restrict__ weight,
                                                                T* __restrict__ out, const int* __restrict__ order) {
   using S = Slice<T, 16>;
-  constexpr int kCh = S::kChannels, kPairs = S::kPairs, kWords = 4;
-  constexpr int C = Chunk<G, 8>::kSamples, kOwn = Chunk<G, 8>::kStagerStride;
+  constexpr int kCh = S::kChannels, kPairs = S::kPairs;
   extern __shared__ Level levels[];
-  __shared__ int4 s_row[kCtaThreads];
-  __shared__ float4 s_wa[kCtaThreads];
+  __shared__ int4 s_row[FwdSlots<G>::kTotal];
+  __shared__ float4 s_wa[FwdSlots<G>::kTotal];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
-  const int base = threadIdx.x - sub;
-  const bool stager = sub % kOwn == 0;
-  const int mine = sub / kOwn;
+  const int base = (threadIdx.x / G) * FwdSlots<G>::kPerGroup;
   constexpr int kGroups = kCtaThreads / G;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int row_stride = d.heads * d.channels;  // elements between neighbouring pixels
   const int samples = d.levels * d.points;
 
   // Whole warps take the same number of trips (the trip count depends only on
-  // the warp's first item), so the warp-wide syncs below are convergent.
+  // the warp's first item), so the warp-wide syncs are convergent.
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
   for (int64_t slot = static_cast<int64_t>(blockIdx.x) * kGroups + threadIdx.x / G;
        slot - (threadIdx.x % 32) / G < items; slot += stride) {
@@ -63,49 +122,73 @@ __global__ void __launch_bounds__(kCtaThreads) forward_vec_kernel(Dims d, const 
     const int h = static_cast<int>(item % d.heads);
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
     const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
-    const T* lp = loc + item * samples * 2;
-    const T* wp = weight + item * samples;
-
     float2 acc[kPairs];
-#pragma unroll
-    for (int i = 0; i < kPairs; ++i) acc[i] = make_float2(0.0f, 0.0f);
-
-    for (int s0 = 0; s0 < samples; s0 += C) {
-      if (stager) stage_sample(levels, d.points, samples, live, s0 + mine, lp, wp, s_row + threadIdx.x, s_wa + threadIdx.x);
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < C; ++i) {
-        const int4 r4 = s_row[base + i * kOwn];
-        const float4 w4 = s_wa[base + i * kOwn];
-        const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
-        const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
-        Words<kWords> raw[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          raw[k] = rows[k] >= 0 ? ldg_words<16>(vbase + static_cast<int64_t>(rows[k]) * row_stride) : zero_words<kWords>();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-#if MSDA_FWD_PACKED
-          const float2 w2 = make_float2(wa[k], wa[k]);
-#pragma unroll
-          for (int q = 0; q < kPairs; ++q) acc[q] = ffma2(w2, S::pair(raw[k], q), acc[q]);
-#else
-#pragma unroll
-          for (int q = 0; q < kPairs; ++q) {
-            const float2 v = S::pair(raw[k], q);
-            acc[q].x = fmaf(wa[k], v.x, acc[q].x);
-            acc[q].y = fmaf(wa[k], v.y, acc[q].y);
-          }
-#endif
-        }
-      }
-      __syncwarp();
-    }
+    gather_head_row<T, G>(levels, d.points, samples, live, vbase, row_stride, loc + item * samples * 2,
+                          weight + item * samples, sub, s_row + base, s_wa + base, acc);
     if (live) {
       float f[kCh];
 #pragma unroll
       for (int q = 0; q < kPairs; ++q) f[2 * q] = acc[q].x, f[2 * q + 1] = acc[q].y;
       st16(out + item * d.channels + sub * kCh, Vec16<T>::pack(f));
+    }
+  }
+}
+
+// BEVFormer spatial cross-attention, forward fused with the rebatch scatter
+// and the camera-count normalisation, for one camera: for every batch entry
+// b, rebatched query q < valid_len of camera cam and head h,
+//   slots[b, index[q], h, :] += msda(b * cams + cam, q, h) / count[b, index[q]]
+// (read-modify-write in the storage dtype: index holds distinct BEV queries,
+// so no two items of a launch share a slot row). Locations / weights are the
+// rebatched (B * cams, max_len, Hh, L, P[, 2]) tensors; an index outside
+// [0, num_query) leaves its rows untouched.
+template <typename T, int G>
+__global__ void __launch_bounds__(kCtaThreads) scatter_div_vec_kernel(
+    Dims d, SlotDims sd, const T* __restrict__ value, const int64_t* __restrict__ shapes,
+    const int64_t* __restrict__ starts, const T* __restrict__ loc, const T* __restrict__ weight,
+    const int64_t* __restrict__ index, const T* __restrict__ count, T* __restrict__ slots) {
+  using S = Slice<T, 16>;
+  constexpr int kCh = S::kChannels, kPairs = S::kPairs;
+  extern __shared__ Level levels[];
+  __shared__ int4 s_row[FwdSlots<G>::kTotal];
+  __shared__ float4 s_wa[FwdSlots<G>::kTotal];
+  stage_levels(levels, shapes, starts, d);
+
+  const int sub = threadIdx.x % G;
+  const int base = (threadIdx.x / G) * FwdSlots<G>::kPerGroup;
+  constexpr int kGroups = kCtaThreads / G;
+  const int64_t items = static_cast<int64_t>(sd.batch) * sd.valid_len * d.heads;
+  const int row_stride = d.heads * d.channels;
+  const int samples = d.levels * d.points;
+
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
+  for (int64_t slot = static_cast<int64_t>(blockIdx.x) * kGroups + threadIdx.x / G;
+       slot - (threadIdx.x % 32) / G < items; slot += stride) {
+    const bool live = slot < items;
+    const int64_t item = live ? slot : items - 1;
+    const int h = static_cast<int>(item % d.heads);
+    const int64_t bq = item / d.heads;
+    const int64_t q = bq % sd.valid_len;
+    const int64_t b = bq / sd.valid_len;
+    const int64_t image = b * sd.cams + sd.cam;
+    const int64_t lrow = (image * d.queries + q) * d.heads + h;  // rebatched (image, q, h) row
+    const T* vbase = value + (image * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
+    float2 acc[kPairs];
+    gather_head_row<T, G>(levels, d.points, samples, live, vbase, row_stride, loc + lrow * samples * 2,
+                          weight + lrow * samples, sub, s_row + base, s_wa + base, acc);
+    const int64_t bev = index[q];
+    if (live && bev >= 0 && bev < sd.num_query) {
+      const int64_t srow = b * sd.num_query + bev;
+      const float inv = 1.0f / to_f32(count[srow]);
+      T* dst = slots + (srow * d.heads + h) * d.channels + sub * kCh;
+      float f[kCh];
+      Vec16<T>::unpack(*reinterpret_cast<const uint4*>(dst), f);
+#pragma unroll
+      for (int q2 = 0; q2 < kPairs; ++q2) {
+        f[2 * q2] += acc[q2].x * inv;
+        f[2 * q2 + 1] += acc[q2].y * inv;
+      }
+      st16(dst, Vec16<T>::pack(f));
     }
   }
 }
@@ -182,6 +265,42 @@ static cudaError_t launch_forward_t(const Dims& d, const Args& a, cudaStream_t s
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<T*>(a.out));
   return cudaGetLastError();
+}
+
+template <typename T, int G>
+static cudaError_t launch_scatter_div_vec(const Dims& d, const SlotDims& sd, const Args& a, const int64_t* index,
+                                         const void* count, void* slots, cudaStream_t stream) {
+  const int64_t items = static_cast<int64_t>(sd.batch) * sd.valid_len * d.heads;
+  const int64_t groups_per_cta = kCtaThreads / G;
+  const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
+  const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
+  scatter_div_vec_kernel<T, G><<<grid, kCtaThreads, level_smem(d), stream>>>(
+      d, sd, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
+      static_cast<const T*>(a.weight), index, static_cast<const T*>(count), static_cast<T*>(slots));
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_scatter_div_t(const Dims& d, const SlotDims& sd, const Args& a, const int64_t* index,
+                                       const void* count, void* slots, cudaStream_t stream) {
+  Args probe = a;
+  probe.out = slots;  // the slot rows are read and written in 16-byte lane slices
+  switch (vec_group(d.channels, sizeof(T), probe)) {
+    case 1: return launch_scatter_div_vec<T, 1>(d, sd, a, index, count, slots, stream);
+    case 2: return launch_scatter_div_vec<T, 2>(d, sd, a, index, count, slots, stream);
+    case 4: return launch_scatter_div_vec<T, 4>(d, sd, a, index, count, slots, stream);
+    case 8: return launch_scatter_div_vec<T, 8>(d, sd, a, index, count, slots, stream);
+    case 16: return launch_scatter_div_vec<T, 16>(d, sd, a, index, count, slots, stream);
+    case 32: return launch_scatter_div_vec<T, 32>(d, sd, a, index, count, slots, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_scatter_div(DType dtype, const Dims& d, const SlotDims& sd, const Args& a, const int64_t* index,
+                               const void* count, void* slots, cudaStream_t stream) {
+  if (sd.batch == 0 || sd.valid_len == 0 || d.heads == 0) return cudaSuccess;
+  return dtype == DType::kBF16 ? launch_scatter_div_t<__nv_bfloat16>(d, sd, a, index, count, slots, stream)
+                               : launch_scatter_div_t<float>(d, sd, a, index, count, slots, stream);
 }
 
 cudaError_t launch_forward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream) {

@@ -17,6 +17,13 @@ struct Level {
 
 enum class DType { kF32 = 0, kBF16 = 1 };
 
+// The rebatch side of the fused spatial-cross-attention scatter (one camera):
+// batch entries, cameras per batch entry, the camera, its valid rebatched
+// queries and the BEV queries of the slots tensor.
+struct SlotDims {
+  int batch, cams, cam, valid_len, num_query;
+};
+
 // Raw device pointers of one call. Forward uses value..out; backward uses
 // value..weight, grad_out and the three gradient buffers.
 struct Args {
@@ -90,5 +97,12 @@ cudaError_t static_scratch_address(void** out);
 // channel count (msda_forward.cu, msda_backward.cu).
 cudaError_t launch_forward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 cudaError_t launch_backward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
+
+// Fused MSDA forward + rebatch scatter + count normalisation for one camera
+// (msda_forward.cu); d describes the rebatched call (batch = B * cams,
+// queries = max_len). cudaErrorInvalidValue when the channel count has no
+// 16-byte lane layout.
+cudaError_t launch_scatter_div(DType dtype, const Dims& d, const SlotDims& sd, const Args& a, const int64_t* index,
+                               const void* count, void* slots, cudaStream_t stream);
 
 }  // namespace msda

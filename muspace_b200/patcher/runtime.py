@@ -259,6 +259,108 @@ class DefaultPatcher:
         return patched
 
 
-default_patcher = DefaultPatcher()
+# Qwen-Drive's perception head (patcher/runtime.py:77-81 of the reference)
+QWENDRIVE_ATTENTION_MODULE = "qwen_drive_perception.attention"
+QWENDRIVE_MSDA_ATTR = "multi_scale_deformable_attn_cuda"
+QWENDRIVE_OPS_MODULE = "qwen_drive_perception.ops"
+QWENDRIVE_MSDA_FORWARD_ATTR = "ms_deform_attn_bf16_forward"
 
-__all__ = ["DefaultPatcher", "PatchError", "PatchReport", "default_patcher"]
+
+def _make_qwendrive_msda_wrapper(strict: bool, original: PatchCallable) -> PatchCallable:
+    """Six-argument Qwen-Drive MSDA entry (reference ``patcher/runtime.py:285-337``).
+
+    Qwen-Drive calls ``(value, spatial_shapes, level_start_index, locations,
+    weights, im2col_step)`` and its own kernel is bfloat16-only and forward-only.
+    CUDA tensors go through the native autograd operator (forward and
+    backward); a CUDA tensor that is not bfloat16 raises, as Qwen-Drive's gate
+    does; anything else keeps Qwen-Drive's original function.
+    """
+
+    backend = "cuda" if strict else "auto"
+
+    def muspace_qwendrive_msda(value, value_spatial_shapes, value_level_start_index, sampling_locations,
+                               attention_weights, im2col_step):
+        if not _is_cuda(value):
+            return original(value, value_spatial_shapes, value_level_start_index, sampling_locations,
+                            attention_weights, im2col_step)
+        import torch
+
+        if value.dtype != torch.bfloat16:
+            raise TypeError(
+                "the ms_deform_attn kernel requires bfloat16 tensors on CUDA, "
+                f"got {value.dtype}; run the model in bfloat16"
+            )
+        from muspace_b200.ops import multi_scale_deformable_attn
+
+        return multi_scale_deformable_attn(value, value_spatial_shapes, value_level_start_index, sampling_locations,
+                                           attention_weights, im2col_step=int(im2col_step), backend=backend)
+
+    muspace_qwendrive_msda.__name__ = "muspace_qwendrive_msda_strict" if strict else "muspace_qwendrive_msda"
+    muspace_qwendrive_msda.__module__ = __name__
+    return muspace_qwendrive_msda
+
+
+class QwenDrivePatcher:
+    """Route Qwen-Drive's multi-scale deformable attention onto the B200 operator.
+
+    Reference: ``QwenDrivePatcher`` (``patcher/runtime.py:1897-2018``). It rebinds
+    ``qwen_drive_perception.attention.multi_scale_deformable_attn_cuda`` and
+    ``qwen_drive_perception.ops.ms_deform_attn_bf16_forward`` to one wrapper,
+    which adds the backward Qwen-Drive's forward-only kernel lacks. The
+    reference also replaces ``ops.voxel_pool_depth`` and the view transform's
+    ``frustum`` property because Qwen-Drive's CUDA code cannot run on MUSA; on
+    a CUDA GPU that code runs as shipped, so this patcher leaves both alone.
+    """
+
+    def __init__(self) -> None:
+        self._originals: dict[tuple[str, str], object] = {}
+        self._strict: bool | None = None
+
+    def apply(self, *, strict: bool | None = None) -> PatchReport:
+        strict = _env_strict() if strict is None else strict
+        attention, ops = self._import_package()
+        missing = [f"{QWENDRIVE_ATTENTION_MODULE}.{QWENDRIVE_MSDA_ATTR}"] if not callable(
+            getattr(attention, QWENDRIVE_MSDA_ATTR, None)) else []
+        if not callable(getattr(ops, QWENDRIVE_MSDA_FORWARD_ATTR, None)):
+            missing.append(f"{QWENDRIVE_OPS_MODULE}.{QWENDRIVE_MSDA_FORWARD_ATTR}")
+        if missing:
+            raise PatchError(
+                "qwen_drive_perception is missing the symbols this patcher replaces: " + ", ".join(missing)
+            )
+        # a second apply keeps Qwen-Drive's own function as the fallback
+        original = self._originals.get((attention.__name__, QWENDRIVE_MSDA_ATTR),
+                                       getattr(attention, QWENDRIVE_MSDA_ATTR))
+        wrapper = _make_qwendrive_msda_wrapper(strict, original)
+        patched = []
+        if _patch_attr(self._originals, attention, QWENDRIVE_MSDA_ATTR, wrapper):
+            patched.append(attention.__name__)
+        if _patch_attr(self._originals, ops, QWENDRIVE_MSDA_FORWARD_ATTR, wrapper):
+            patched.append(ops.__name__)
+        action = "already-applied" if self._strict == strict else "applied"
+        self._strict = strict
+        return PatchReport(target=f"{QWENDRIVE_ATTENTION_MODULE}.{QWENDRIVE_MSDA_ATTR}", strict=strict,
+                           action=action, patched_modules=tuple(patched))
+
+    def restore(self) -> PatchReport:
+        restored = _restore_attrs(self._originals)
+        self._strict = None
+        return PatchReport(target=f"{QWENDRIVE_ATTENTION_MODULE}.{QWENDRIVE_MSDA_ATTR}", strict=False,
+                           action="restored", patched_modules=tuple(restored))
+
+    @staticmethod
+    def _import_package() -> tuple[ModuleType, ModuleType]:
+        try:
+            attention = importlib.import_module(QWENDRIVE_ATTENTION_MODULE)
+            ops = importlib.import_module(QWENDRIVE_OPS_MODULE)
+        except ImportError as exc:
+            raise PatchError(
+                "qwen_drive_perception import failed. Add the Qwen-Drive checkout src "
+                "directory to PYTHONPATH before qwendrive_patcher.apply()."
+            ) from exc
+        return attention, ops
+
+
+default_patcher = DefaultPatcher()
+qwendrive_patcher = QwenDrivePatcher()
+
+__all__ = ["DefaultPatcher", "PatchError", "PatchReport", "QwenDrivePatcher", "default_patcher", "qwendrive_patcher"]

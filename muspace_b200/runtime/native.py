@@ -107,6 +107,7 @@ def _stream_of(tensors) -> int:
 _SIGNATURES: dict[str, tuple[str, ...]] = {
     "ms_deform_attn_forward": ("t",) * 6 + ("i",),
     "ms_deform_attn_backward": ("t",) * 9 + ("i",),
+    "ms_deform_attn_scatter_div_forward": ("t",) * 8 + ("i",),
 }
 
 

@@ -112,3 +112,4 @@ def test_static_scratch_backward_rejects_problems_beyond_its_array():
     aligned = ctypes.c_void_p(256)  # never dereferenced: the size check fails first
     assert fn(1, ctypes.byref(dims), *([aligned] * 9), None) == 1
     assert "bytes of scratch" in native.load_native_module().last_error()
+

@@ -136,3 +136,130 @@ def test_legacy_extension_guard_returns_placeholder_for_failed_load(monkeypatch)
     with pytest.raises(PatchError, match="mmcv._ext is unavailable"):
         placeholder.nms()
     patcher.restore()
+
+
+# ---------------------------------------------------------------------------------------
+# Qwen-Drive (reference tests/test_runtime_patcher.py:125-290, MSDA part)
+# ---------------------------------------------------------------------------------------
+
+
+def _install_fake_qwendrive(monkeypatch):
+    attention = types.ModuleType("qwen_drive_perception.attention")
+    ops = types.ModuleType("qwen_drive_perception.ops")
+
+    def original_msda(*args, **kwargs):
+        return ("pytorch", args, kwargs)
+
+    def original_forward(*args, **kwargs):
+        return "forward-only"
+
+    def original_pool(*args, **kwargs):
+        return "upstream-pool"
+
+    attention.multi_scale_deformable_attn_cuda = original_msda
+    ops.ms_deform_attn_bf16_forward = original_forward
+    ops.voxel_pool_depth = original_pool
+    for module in (attention, ops):
+        monkeypatch.setitem(sys.modules, module.__name__, module)
+    return attention, ops, original_msda, original_forward, original_pool
+
+
+def test_qwendrive_patcher_rebinds_and_restores(monkeypatch):
+    from mu_space.patcher import QwenDrivePatcher
+
+    attention, ops, msda, forward, pool = _install_fake_qwendrive(monkeypatch)
+    patcher = QwenDrivePatcher()
+    first = patcher.apply()
+    assert first.action == "applied" and first.strict is False
+    assert attention.multi_scale_deformable_attn_cuda is not msda
+    assert ops.ms_deform_attn_bf16_forward is attention.multi_scale_deformable_attn_cuda
+    assert ops.voxel_pool_depth is pool  # Qwen-Drive's own CUDA code runs on CUDA GPUs
+    assert patcher.apply().action == "already-applied"
+    cpu = types.SimpleNamespace(dtype=torch.float32, device=types.SimpleNamespace(type="cpu"))
+    assert attention.multi_scale_deformable_attn_cuda(cpu, 1, 2, 3, 4, 64)[0] == "pytorch"
+    restored = patcher.restore()
+    assert restored.action == "restored"
+    assert attention.multi_scale_deformable_attn_cuda is msda
+    assert ops.ms_deform_attn_bf16_forward is forward
+    patcher.restore()
+    assert attention.multi_scale_deformable_attn_cuda is msda
+
+
+def test_qwendrive_msda_wrapper_routes_by_device(monkeypatch):
+    from mu_space.patcher import QwenDrivePatcher
+
+    attention, ops, *_rest = _install_fake_qwendrive(monkeypatch)
+    captured = {}
+
+    def fake_msda(*args, **kwargs):
+        captured["args"], captured["kwargs"] = args, kwargs
+        return "native"
+
+    monkeypatch.setattr("muspace_b200.ops.multi_scale_deformable_attn", fake_msda)
+    patcher = QwenDrivePatcher()
+    patcher.apply()
+    wrapper = attention.multi_scale_deformable_attn_cuda
+    cuda = types.SimpleNamespace(dtype=torch.bfloat16, device=types.SimpleNamespace(type="cuda"))
+    assert wrapper(cuda, "shapes", "starts", "locations", "weights", im2col_step=64) == "native"
+    assert captured["kwargs"] == {"im2col_step": 64, "backend": "auto"}
+    assert captured["args"][1:] == ("shapes", "starts", "locations", "weights")
+    with pytest.raises(TypeError, match="bfloat16"):
+        wrapper(types.SimpleNamespace(dtype=torch.float32, device=types.SimpleNamespace(type="cuda")),
+                None, None, None, None, 64)
+    cpu = types.SimpleNamespace(dtype=torch.float32, device=types.SimpleNamespace(type="cpu"))
+    assert wrapper(cpu, "shapes", "starts", "locations", "weights", 64)[0] == "pytorch"
+    assert ops.ms_deform_attn_bf16_forward is wrapper
+    patcher.restore()
+    patcher.apply(strict=True)
+    attention.multi_scale_deformable_attn_cuda(cuda, "s", "t", "l", "w", 32)
+    assert captured["kwargs"] == {"im2col_step": 32, "backend": "cuda"}
+    patcher.restore()
+
+
+def test_qwendrive_patcher_rejects_a_partial_package(monkeypatch):
+    from mu_space.patcher import QwenDrivePatcher
+
+    attention, ops, *_rest = _install_fake_qwendrive(monkeypatch)
+    del ops.ms_deform_attn_bf16_forward
+    with pytest.raises(PatchError, match="ms_deform_attn_bf16_forward"):
+        QwenDrivePatcher().apply()
+    assert attention.multi_scale_deformable_attn_cuda(None)[0] == "pytorch"
+
+
+def test_qwendrive_patcher_without_the_package_is_a_patch_error(monkeypatch):
+    from mu_space.patcher import QwenDrivePatcher
+
+    monkeypatch.setitem(sys.modules, "qwen_drive_perception", None)
+    monkeypatch.delitem(sys.modules, "qwen_drive_perception.attention", raising=False)
+    with pytest.raises(PatchError, match="PYTHONPATH"):
+        QwenDrivePatcher().apply()
+
+
+@pytest.mark.gpu
+def test_qwendrive_wrapper_runs_forward_and_backward_on_the_b200_kernels(monkeypatch, cuda_device):
+    """Qwen-Drive's kernel is forward-only; through the wrapper its bf16 MSDA
+    gets gradients, equal to the fp32 oracle on the same quantised inputs."""
+    from mu_space.patcher import QwenDrivePatcher
+    from muspace_b200 import cases
+    from oracle import oracle_backward, oracle_forward
+
+    attention, *_rest = _install_fake_qwendrive(monkeypatch)
+    patcher = QwenDrivePatcher()
+    patcher.apply()
+    try:
+        cfg = cases.CONFIGS["c2"].with_(batch=1, queries=64)
+        inp = cases.make_inputs(cfg, dtype=torch.bfloat16, device=cuda_device)
+        names = ("value", "spatial_shapes", "level_start_index", "sampling_locations", "attention_weights")
+        leaves = {k: (inp[k].clone().requires_grad_(True) if inp[k].is_floating_point() else inp[k]) for k in names}
+        out = attention.multi_scale_deformable_attn_cuda(*[leaves[k] for k in names], 64)
+        out.backward(inp["grad_output"])
+        host = [inp[k].float().cpu().numpy() if inp[k].is_floating_point() else inp[k].cpu().numpy() for k in names]
+        exp_out = oracle_forward(*host)
+        _, exp_gl, exp_gw = oracle_backward(*host, inp["grad_output"].float().cpu().numpy())
+        torch.testing.assert_close(out.float().cpu(), torch.from_numpy(exp_out), rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(leaves["sampling_locations"].grad.float().cpu(), torch.from_numpy(exp_gl),
+                                   rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(leaves["attention_weights"].grad.float().cpu(), torch.from_numpy(exp_gw),
+                                   rtol=2e-2, atol=2e-2)
+    finally:
+        patcher.restore()
