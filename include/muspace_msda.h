@@ -235,6 +235,51 @@ MSDA_API int msda_scatter_div_forward(msda_dtype_t dtype, const msda_dims_t *dim
                                       const void *attention_weights, const int64_t *index, const void *count,
                                       void *slots, void *stream);
 
+/*
+ * SparseDrive deformable aggregation (multi-camera, multi-scale feature
+ * gather with per-group weights), float32:
+ *
+ *   output[b, a, :] = sum over (pt, cam) whose sampling_location lies in the
+ *                     open square (0, 1)^2, and over scales s, of
+ *                     weights[b, a, pt, cam, s, group] * bilinear(map(cam, s), location)
+ *
+ * with the bilinear sample at h = y * H - 0.5, w = x * W - 0.5 and corners
+ * outside the map read as zero. Layouts (contiguous):
+ *   mc_ms_feat          [B, num_feat, C]                  float32
+ *   spatial_shape       [num_cams, num_scale, 2]          int32 (H, W)
+ *   scale_start_index   [num_cams, num_scale]             int32 (first row of each map)
+ *   sampling_location   [B, anchors, pts, num_cams, 2]    float32 (x, y)
+ *   weights             [B, anchors, pts, num_cams, num_scale, groups], 1 <= groups <= 8, C % groups == 0
+ *   output              [B, anchors, C]                   float32, overwritten
+ *
+ * Replace the reference exports of the same names and argument order
+ * (csrc/deformable_aggregation/deformable_aggregation_musa.mu:718-751;
+ * `stream` is new). *_opt run the warp-per-anchor kernels when
+ * C % 4 == 0, C <= 512, C / groups is 4 times a power of two and the float
+ * tensors are 16-byte aligned, the scalar kernels otherwise; *_base always run
+ * the scalar kernels (the reference's baseline pair, kept for comparison).
+ *
+ * Backward: grad_mc_ms_feat is ACCUMULATED into (the caller zeroes it, as the
+ * reference's Python layer does); grad_sampling_location and grad_weights are
+ * written for every entry (zero where the location is outside the image).
+ */
+MSDA_API int deformable_aggregation_forward_opt(const DLTensor *mc_ms_feat, const DLTensor *spatial_shape,
+                                                const DLTensor *scale_start_index, const DLTensor *sampling_location,
+                                                const DLTensor *weights, DLTensor *output, void *stream);
+MSDA_API int deformable_aggregation_forward_base(const DLTensor *mc_ms_feat, const DLTensor *spatial_shape,
+                                                 const DLTensor *scale_start_index, const DLTensor *sampling_location,
+                                                 const DLTensor *weights, DLTensor *output, void *stream);
+MSDA_API int deformable_aggregation_backward_opt(const DLTensor *mc_ms_feat, const DLTensor *spatial_shape,
+                                                 const DLTensor *scale_start_index, const DLTensor *sampling_location,
+                                                 const DLTensor *weights, const DLTensor *grad_output,
+                                                 DLTensor *grad_mc_ms_feat, DLTensor *grad_sampling_location,
+                                                 DLTensor *grad_weights, void *stream);
+MSDA_API int deformable_aggregation_backward_base(const DLTensor *mc_ms_feat, const DLTensor *spatial_shape,
+                                                  const DLTensor *scale_start_index, const DLTensor *sampling_location,
+                                                  const DLTensor *weights, const DLTensor *grad_output,
+                                                  DLTensor *grad_mc_ms_feat, DLTensor *grad_sampling_location,
+                                                  DLTensor *grad_weights, void *stream);
+
 /* Message of the last failed call on this thread ("" after a success). The
  * reference raised it as a TVM-FFI exception (csrc/ffi/tensor_utils.hpp:13-34). */
 MSDA_API const char *msda_last_error(void);

@@ -18,6 +18,7 @@ _SUBMODULES = (
     "ops",
     "ops.multi_scale_deformable_attn",
     "ops.sca_scatter",
+    "ops.deformable_aggregation",
     "runtime",
     "runtime.kernel_dispatch",
     "runtime.native",

@@ -14,6 +14,7 @@
 #include <string>
 
 #include "../../include/muspace_msda.h"
+#include "deform_agg.h"
 #include "msda_kernels.h"
 
 namespace {
@@ -419,6 +420,129 @@ int msda_scatter_div_forward(msda_dtype_t dtype, const msda_dims_t* dims, const 
             "msda_scatter_div_forward needs Hh * D rows in 16-byte lane slices and 16-byte aligned pointers");
     check_launch(err, "msda_scatter_div_forward");
   });
+}
+
+// ---------------------------------------------------------------------------
+// deformable aggregation (csrc/deformable_aggregation/deformable_aggregation_musa.mu:643-751)
+// ---------------------------------------------------------------------------
+namespace {
+
+struct DaViews {
+  da::Dims dims;
+  da::Args args;
+  int device;
+};
+
+// The reference's validate() (fp32 / int32, contiguous, ranks) plus the shape
+// agreements it left to the Python layer (mu_space/ops/deformable_aggregation.py:35-79).
+DaViews da_views(const DLTensor* mc, const DLTensor* sp, const DLTensor* st, const DLTensor* loc, const DLTensor* w) {
+  require(mc != nullptr, "mc_ms_feat is null");
+  const int dev = mc->device.device_id;
+  check_tensor(mc, "mc_ms_feat", kDLFloat, 32, 3, dev);
+  check_tensor(sp, "spatial_shape", kDLInt, 32, 3, dev);
+  check_tensor(st, "scale_start_index", kDLInt, 32, 2, dev);
+  check_tensor(loc, "sampling_location", kDLFloat, 32, 5, dev);
+  check_tensor(w, "weights", kDLFloat, 32, 6, dev);
+  const int64_t batch = mc->shape[0], num_feat = mc->shape[1], channels = mc->shape[2];
+  const int64_t cams = sp->shape[0], scales = sp->shape[1];
+  const int64_t anchors = loc->shape[1], pts = loc->shape[2], groups = w->shape[5];
+  require(sp->shape[2] == 2, "spatial_shape must have shape [num_cams, num_scale, 2]");
+  require(st->shape[0] == cams && st->shape[1] == scales, "scale_start_index must have shape [num_cams, num_scale]");
+  require(loc->shape[0] == batch && loc->shape[3] == cams && loc->shape[4] == 2,
+          "sampling_location must have shape [B, anchors, pts, cams, 2]");
+  require(w->shape[0] == batch && w->shape[1] == anchors && w->shape[2] == pts && w->shape[3] == cams &&
+              w->shape[4] == scales,
+          "weights must have shape [B, anchors, pts, cams, scale, groups]");
+  require(groups >= 1 && groups <= 8, "num_groups must be in [1, 8]");
+  require(channels % groups == 0, "num_embeds must be divisible by num_groups");
+  const int64_t kMax = std::numeric_limits<int32_t>::max();
+  require(batch <= kMax && num_feat <= kMax && channels <= kMax && anchors <= kMax && pts <= 65536,
+          "a size exceeds the supported range");
+  require(cams * scales <= 1024 && pts * cams <= kMax, "num_cams * num_scale exceeds 1024");
+  DaViews v{};
+  v.dims = da::Dims{static_cast<int>(batch), static_cast<int>(num_feat), static_cast<int>(channels),
+                    static_cast<int>(cams), static_cast<int>(scales), static_cast<int>(anchors),
+                    static_cast<int>(pts), static_cast<int>(groups)};
+  v.args.feat = static_cast<const float*>(data_of(mc));
+  v.args.shape = static_cast<const int*>(data_of(sp));
+  v.args.start = static_cast<const int*>(data_of(st));
+  v.args.loc = static_cast<const float*>(data_of(loc));
+  v.args.weights = static_cast<const float*>(data_of(w));
+  v.device = dev;
+  return v;
+}
+
+int da_forward_entry(const DLTensor* mc, const DLTensor* sp, const DLTensor* st, const DLTensor* loc,
+                     const DLTensor* w, DLTensor* out, void* stream, bool optimized, const char* name) {
+  return guarded([&] {
+    DaViews v = da_views(mc, sp, st, loc, w);
+    check_tensor(out, "out", kDLFloat, 32, 3, v.device);
+    require(out->shape[0] == mc->shape[0] && out->shape[1] == loc->shape[1] && out->shape[2] == mc->shape[2],
+            "out must have shape [B, anchors, C]");
+    v.args.out = static_cast<float*>(data_of(out));
+    DeviceGuard guard(v.device);
+    check_launch(da::forward(v.dims, v.args, optimized, static_cast<cudaStream_t>(stream)), name);
+  });
+}
+
+int da_backward_entry(const DLTensor* mc, const DLTensor* sp, const DLTensor* st, const DLTensor* loc,
+                      const DLTensor* w, const DLTensor* grad, DLTensor* grad_mc, DLTensor* grad_loc,
+                      DLTensor* grad_w, void* stream, bool optimized, const char* name) {
+  return guarded([&] {
+    DaViews v = da_views(mc, sp, st, loc, w);
+    check_tensor(grad, "grad_output", kDLFloat, 32, 3, v.device);
+    check_tensor(grad_mc, "grad_mc_ms_feat", kDLFloat, 32, 3, v.device);
+    check_tensor(grad_loc, "grad_sampling_location", kDLFloat, 32, 5, v.device);
+    check_tensor(grad_w, "grad_weights", kDLFloat, 32, 6, v.device);
+    require(grad->shape[0] == mc->shape[0] && grad->shape[1] == loc->shape[1] && grad->shape[2] == mc->shape[2],
+            "grad_output must have shape [B, anchors, C]");
+    for (int i = 0; i < 3; ++i) require(grad_mc->shape[i] == mc->shape[i], "grad_mc_ms_feat must have the shape of mc_ms_feat");
+    for (int i = 0; i < 5; ++i)
+      require(grad_loc->shape[i] == loc->shape[i], "grad_sampling_location must have the shape of sampling_location");
+    for (int i = 0; i < 6; ++i) require(grad_w->shape[i] == w->shape[i], "grad_weights must have the shape of weights");
+    v.args.grad_out = static_cast<const float*>(data_of(grad));
+    v.args.grad_feat = static_cast<float*>(data_of(grad_mc));
+    v.args.grad_loc = static_cast<float*>(data_of(grad_loc));
+    v.args.grad_weights = static_cast<float*>(data_of(grad_w));
+    DeviceGuard guard(v.device);
+    check_launch(da::backward(v.dims, v.args, optimized, static_cast<cudaStream_t>(stream)), name);
+  });
+}
+
+}  // namespace
+
+int deformable_aggregation_forward_opt(const DLTensor* mc_ms_feat, const DLTensor* spatial_shape,
+                                       const DLTensor* scale_start_index, const DLTensor* sampling_location,
+                                       const DLTensor* weights, DLTensor* output, void* stream) {
+  return da_forward_entry(mc_ms_feat, spatial_shape, scale_start_index, sampling_location, weights, output, stream,
+                          true, "deformable_aggregation_forward_opt");
+}
+
+int deformable_aggregation_forward_base(const DLTensor* mc_ms_feat, const DLTensor* spatial_shape,
+                                        const DLTensor* scale_start_index, const DLTensor* sampling_location,
+                                        const DLTensor* weights, DLTensor* output, void* stream) {
+  return da_forward_entry(mc_ms_feat, spatial_shape, scale_start_index, sampling_location, weights, output, stream,
+                          false, "deformable_aggregation_forward_base");
+}
+
+int deformable_aggregation_backward_opt(const DLTensor* mc_ms_feat, const DLTensor* spatial_shape,
+                                        const DLTensor* scale_start_index, const DLTensor* sampling_location,
+                                        const DLTensor* weights, const DLTensor* grad_output,
+                                        DLTensor* grad_mc_ms_feat, DLTensor* grad_sampling_location,
+                                        DLTensor* grad_weights, void* stream) {
+  return da_backward_entry(mc_ms_feat, spatial_shape, scale_start_index, sampling_location, weights, grad_output,
+                           grad_mc_ms_feat, grad_sampling_location, grad_weights, stream, true,
+                           "deformable_aggregation_backward_opt");
+}
+
+int deformable_aggregation_backward_base(const DLTensor* mc_ms_feat, const DLTensor* spatial_shape,
+                                         const DLTensor* scale_start_index, const DLTensor* sampling_location,
+                                         const DLTensor* weights, const DLTensor* grad_output,
+                                         DLTensor* grad_mc_ms_feat, DLTensor* grad_sampling_location,
+                                         DLTensor* grad_weights, void* stream) {
+  return da_backward_entry(mc_ms_feat, spatial_shape, scale_start_index, sampling_location, weights, grad_output,
+                           grad_mc_ms_feat, grad_sampling_location, grad_weights, stream, false,
+                           "deformable_aggregation_backward_base");
 }
 
 const char* msda_last_error(void) { return g_last_error.c_str(); }

@@ -1,6 +1,12 @@
-"""Canonical operator exports of the B200 build (the MSDA operator and the
-fused spatial-cross-attention scatter built on it)."""
+"""Canonical operator exports of the B200 build: the MSDA operator, the fused
+spatial-cross-attention scatter built on it, and SparseDrive's deformable
+aggregation."""
 
+from .deformable_aggregation import (
+    deformable_aggregation,
+    deformable_aggregation_function,
+    feature_maps_format,
+)
 from .multi_scale_deformable_attn import (
     explain_dispatch,
     multi_scale_deformable_attn,
@@ -9,7 +15,10 @@ from .multi_scale_deformable_attn import (
 from .sca_scatter import ms_deform_attn_scatter_div, sca_rebatch_scatter
 
 __all__ = [
+    "deformable_aggregation",
+    "deformable_aggregation_function",
     "explain_dispatch",
+    "feature_maps_format",
     "ms_deform_attn_scatter_div",
     "multi_scale_deformable_attn",
     "multi_scale_deformable_attn_pytorch_compat",

@@ -360,7 +360,155 @@ class QwenDrivePatcher:
         return attention, ops
 
 
+# SparseDrive's deformable aggregation (patcher/runtime.py:61-70 of the reference)
+SPARSEDRIVE_OPS_MODULE = "projects.mmdet3d_plugin.ops"
+SPARSEDRIVE_DAF_ATTR = "deformable_aggregation_function"
+SPARSEDRIVE_IMPORTED_MODULES = ("projects.mmdet3d_plugin.models.blocks",)
+SPARSEDRIVE_IMPORTED_ATTR = "DAF"
+SPARSEDRIVE_PACKAGE = "projects"
+SPARSEDRIVE_DAF_VALID_ATTR = "DAF_VALID"
+SPARSEDRIVE_FEATURE_MAPS_ATTR = "feature_maps_format"
+SPARSEDRIVE_EXT_MODULE = "projects.mmdet3d_plugin.ops.deformable_aggregation_ext"
+SPARSEDRIVE_EXT_ATTR = "deformable_aggregation_ext"
+
+
+def _make_deformable_aggregation_wrapper(strict: bool) -> PatchCallable:
+    """SparseDrive's five-argument DAF entry (reference ``patcher/runtime.py:519-546``)."""
+    backend = "cuda" if strict else "auto"
+
+    def muspace_deformable_aggregation(feature_maps, spatial_shape, scale_start_index, sampling_location, weights):
+        from muspace_b200.ops import deformable_aggregation_function
+
+        return deformable_aggregation_function(feature_maps, spatial_shape, scale_start_index, sampling_location,
+                                               weights, backend=backend)
+
+    muspace_deformable_aggregation.__name__ = (
+        "muspace_deformable_aggregation_strict" if strict else "muspace_deformable_aggregation_compat"
+    )
+    muspace_deformable_aggregation.__module__ = __name__
+    return muspace_deformable_aggregation
+
+
+class _MissingSparseDriveExtension(ModuleType):
+    """Stands in for SparseDrive's unbuilt CUDA extension so its ops package
+    imports; every use of it raises (the patched entry point never reaches it)."""
+
+    def __getattr__(self, attr: str) -> object:
+        if attr.startswith("__"):
+            raise AttributeError(attr)
+        raise PatchError(
+            f"SparseDrive extension {SPARSEDRIVE_EXT_MODULE} is unavailable; the muSPACE-B200 "
+            "runtime patch routes deformable aggregation to its own kernels"
+        )
+
+
+class SparseDrivePatcher:
+    """Route SparseDrive's deformable aggregation onto the B200 operator.
+
+    Reference: ``SparseDrivePatcher`` (``patcher/runtime.py:1292-1520``), DAF part:
+    rebinds ``projects.mmdet3d_plugin.ops.deformable_aggregation_function`` and
+    the ``DAF`` global of ``projects.mmdet3d_plugin.models.blocks``, lets the ops
+    package import when its CUDA extension was never built, and flips the
+    ``DAF_VALID`` flags that modules cached while the extension was missing. The
+    reference's MATE / flash-attention bridge and its ``Tensor.cuda`` shim exist
+    because SparseDrive's CUDA code cannot run on MUSA; on a CUDA GPU it runs as
+    shipped, so this patcher leaves them alone.
+    """
+
+    def __init__(self) -> None:
+        self._originals: dict[tuple[str, str], object] = {}
+        self._strict: bool | None = None
+        self._placeholder: ModuleType | None = None
+
+    def apply(self, *, strict: bool | None = None) -> PatchReport:
+        strict = _env_strict() if strict is None else strict
+        wrapper = _make_deformable_aggregation_wrapper(strict)
+        target = self._import_ops()
+        try:
+            if not self._patch(target, SPARSEDRIVE_DAF_ATTR, wrapper):
+                raise PatchError(f"{SPARSEDRIVE_OPS_MODULE}.{SPARSEDRIVE_DAF_ATTR} is unavailable")
+            patched = [target.__name__]
+            for module_name in SPARSEDRIVE_IMPORTED_MODULES:
+                module = sys.modules.get(module_name)
+                if module is not None and self._patch(module, SPARSEDRIVE_IMPORTED_ATTR, wrapper):
+                    patched.append(module_name)
+            # modules that probed the ops import before it worked cached DAF_VALID = False
+            prefix = f"{SPARSEDRIVE_PACKAGE}."
+            for name, module in list(sys.modules.items()):
+                if module is None or not (name == SPARSEDRIVE_PACKAGE or name.startswith(prefix)):
+                    continue
+                if getattr(module, SPARSEDRIVE_DAF_VALID_ATTR, None) is not False:
+                    continue
+                self._bind(module, SPARSEDRIVE_DAF_VALID_ATTR, True)
+                fmt = getattr(target, SPARSEDRIVE_FEATURE_MAPS_ATTR, None)
+                if fmt is not None and not hasattr(module, SPARSEDRIVE_FEATURE_MAPS_ATTR):
+                    self._bind(module, SPARSEDRIVE_FEATURE_MAPS_ATTR, fmt)
+                patched.append(name)
+        except BaseException:
+            _restore_attrs(self._originals)
+            self._release_placeholder()
+            raise
+        action = "already-applied" if self._strict == strict else "applied"
+        self._strict = strict
+        return PatchReport(target=f"{SPARSEDRIVE_OPS_MODULE}.{SPARSEDRIVE_DAF_ATTR}", strict=strict, action=action,
+                           patched_modules=tuple(patched))
+
+    def restore(self) -> PatchReport:
+        restored = _restore_attrs(self._originals)
+        self._release_placeholder()
+        self._strict = None
+        return PatchReport(target=f"{SPARSEDRIVE_OPS_MODULE}.{SPARSEDRIVE_DAF_ATTR}", strict=False,
+                           action="restored", patched_modules=tuple(restored))
+
+    def _patch(self, module: ModuleType, attr: str, replacement: object) -> bool:
+        return _patch_attr(self._originals, module, attr, replacement)
+
+    def _bind(self, module: ModuleType, attr: str, value: object) -> None:
+        """Set an attribute that may not exist yet; restore() deletes it again."""
+        key = (module.__name__, attr)
+        if key not in self._originals:
+            self._originals[key] = getattr(module, attr, _MISSING)
+        setattr(module, attr, value)
+
+    def _import_ops(self) -> ModuleType:
+        try:
+            return importlib.import_module(SPARSEDRIVE_OPS_MODULE)
+        except ImportError as exc:
+            missing = getattr(exc, "name", None) in {SPARSEDRIVE_EXT_MODULE, SPARSEDRIVE_EXT_ATTR} or (
+                SPARSEDRIVE_EXT_ATTR in str(exc))
+            if not missing:
+                raise PatchError(
+                    "SparseDrive ops package import failed. Ensure the SparseDrive checkout is on PYTHONPATH "
+                    f"({exc})"
+                ) from exc
+        if SPARSEDRIVE_EXT_MODULE not in sys.modules:
+            self._placeholder = _MissingSparseDriveExtension(SPARSEDRIVE_EXT_MODULE)
+            sys.modules[SPARSEDRIVE_EXT_MODULE] = self._placeholder
+        try:
+            return importlib.import_module(SPARSEDRIVE_OPS_MODULE)
+        except ImportError as exc:
+            self._release_placeholder()
+            raise PatchError(
+                f"SparseDrive ops package import failed. Ensure the SparseDrive checkout is on PYTHONPATH ({exc})"
+            ) from exc
+
+    def _release_placeholder(self) -> None:
+        placeholder, self._placeholder = self._placeholder, None
+        if placeholder is not None and sys.modules.get(SPARSEDRIVE_EXT_MODULE) is placeholder:
+            del sys.modules[SPARSEDRIVE_EXT_MODULE]
+
+
 default_patcher = DefaultPatcher()
 qwendrive_patcher = QwenDrivePatcher()
+sparsedrive_patcher = SparseDrivePatcher()
 
-__all__ = ["DefaultPatcher", "PatchError", "PatchReport", "QwenDrivePatcher", "default_patcher", "qwendrive_patcher"]
+__all__ = [
+    "DefaultPatcher",
+    "PatchError",
+    "PatchReport",
+    "QwenDrivePatcher",
+    "SparseDrivePatcher",
+    "default_patcher",
+    "qwendrive_patcher",
+    "sparsedrive_patcher",
+]

@@ -86,11 +86,15 @@ def _is_cuda_tensor(tensor: torch.Tensor) -> bool:
     return tensor.device.type == "cuda"
 
 
+_KERNEL_NAMES = {"multi_scale_deformable_attn": "MSDA", "deformable_aggregation": "deformable aggregation"}
+
+
 def explain_dispatch(
     value: torch.Tensor,
     *,
     backend: str = "auto",
     native_available: bool = True,
+    operator: str = "multi_scale_deformable_attn",
 ) -> DispatchDecision:
     device = value.device.type
     if backend == "reference":
@@ -98,13 +102,14 @@ def explain_dispatch(
             "error",
             device,
             "the reference PyTorch backend is not part of the B200 build; "
-            "multi_scale_deformable_attn runs on CUDA tensors only",
+            f"{operator} runs on CUDA tensors only",
         )
     if backend not in {"auto", *NATIVE_BACKENDS}:
         return DispatchDecision("error", device, f"unknown backend: {backend}")
     if not _is_cuda_tensor(value):
+        kernels = _KERNEL_NAMES.get(operator, operator)
         return DispatchDecision(
-            "error", device, f"the B200 MSDA kernels need CUDA tensors; value is on {device}"
+            "error", device, f"the B200 {kernels} kernels need CUDA tensors; value is on {device}"
         )
     if not native_available:
         return DispatchDecision("error", device, "muSPACE-B200 native library is unavailable")

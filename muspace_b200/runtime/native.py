@@ -108,6 +108,10 @@ _SIGNATURES: dict[str, tuple[str, ...]] = {
     "ms_deform_attn_forward": ("t",) * 6 + ("i",),
     "ms_deform_attn_backward": ("t",) * 9 + ("i",),
     "ms_deform_attn_scatter_div_forward": ("t",) * 8 + ("i",),
+    "deformable_aggregation_forward_opt": ("t",) * 6,
+    "deformable_aggregation_forward_base": ("t",) * 6,
+    "deformable_aggregation_backward_opt": ("t",) * 9,
+    "deformable_aggregation_backward_base": ("t",) * 9,
 }
 
 
