@@ -280,6 +280,47 @@ MSDA_API int deformable_aggregation_backward_base(const DLTensor *mc_ms_feat, co
                                                   DLTensor *grad_mc_ms_feat, DLTensor *grad_sampling_location,
                                                   DLTensor *grad_weights, void *stream);
 
+/*
+ * FlashSCA (flash_bevpool_sca): BEVFormer spatial cross-attention without the
+ * rebatching, float32. For every BEV cell (gy x gx) the voxel centre at each of
+ * gz heights is projected into every camera (image = P [x y z 1], depth > 0,
+ * u = row0 / max(depth, eps), landing in [0, W) x [0, H)); the cell's output
+ * channel c sums, over the landing (camera, height) pairs, the levels and the
+ * points of head(c), weight * bilinear(level map, base + offset) with
+ * base = (u / W * w - 0.5, v / H * h - 0.5), zero padding and non-finite
+ * feature values read as 0, divided by the number of cameras in which any
+ * height lands.
+ *   value               [B, N, S, C]                         float32
+ *   projection_matrices [B, N, 3, 4]                         float32
+ *   spatial_shapes      [L, 2] int32 (h, w); level_start_index [L] int32; image_size [2] int32 (H, W)
+ *   sampling_offsets    [B, gy, gx, heads, L, P, gz, 2]      float32 (level pixels)
+ *   attention_weights   [B, gy, gx, heads, L, P, gz]         float32
+ *   out                 [B, gy, gx, C]                       float32, overwritten
+ * Replace the reference exports of the same names and argument order
+ * (csrc/flashbev/flash_bevpool_sca_musa.mu:262-399; `stream` is new). The
+ * backward reads the voxel grid from roi_range [xmin, xmax, ymin, ymax, zmin,
+ * zmax] as the reference does and ACCUMULATES into value_grad,
+ * sampling_offsets_grad and attention_weights_grad (the caller zeroes them).
+ * value_stride_n is validated (1 <= it <= S) but rows are addressed with the
+ * tensor's own S, as the reference's PyTorch path does. Limits: C / heads =
+ * 4 * {1, 2, 4, 8, 16, 32}, N * gz <= 64, L <= 16.
+ */
+MSDA_API int flash_bevpool_sca_forward(const DLTensor *value, const DLTensor *projection_matrices,
+                                       const DLTensor *spatial_shapes, const DLTensor *level_start_index,
+                                       const DLTensor *image_size, const DLTensor *sampling_offsets,
+                                       const DLTensor *attention_weights, DLTensor *out, int num_heads,
+                                       int num_points, int grid_x, int grid_y, int grid_z, float voxel_size_x,
+                                       float voxel_size_y, float voxel_size_z, float voxel_x_min, float voxel_y_min,
+                                       float voxel_z_min, int value_stride_n, float epsilon, void *stream);
+MSDA_API int flash_bevpool_sca_backward(const DLTensor *out_grad, const DLTensor *value,
+                                        const DLTensor *projection_matrices, const DLTensor *spatial_shapes,
+                                        const DLTensor *level_start_index, const DLTensor *image_size,
+                                        const DLTensor *roi_range, const DLTensor *sampling_offsets,
+                                        const DLTensor *attention_weights, DLTensor *value_grad,
+                                        DLTensor *sampling_offsets_grad, DLTensor *attention_weights_grad,
+                                        int num_heads, int num_points, int grid_x, int grid_y, int grid_z,
+                                        int value_stride_n, float epsilon, void *stream);
+
 /* Message of the last failed call on this thread ("" after a success). The
  * reference raised it as a TVM-FFI exception (csrc/ffi/tensor_utils.hpp:13-34). */
 MSDA_API const char *msda_last_error(void);

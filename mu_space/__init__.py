@@ -19,14 +19,22 @@ _SUBMODULES = (
     "ops.multi_scale_deformable_attn",
     "ops.sca_scatter",
     "ops.deformable_aggregation",
+    "ops.flash_sca",
     "runtime",
     "runtime.kernel_dispatch",
     "runtime.native",
     "patcher",
     "patcher.runtime",
 )
+# the reference's module names that differ from this build's
+_RENAMED = {"ops.flashbev": "ops.flash_sca"}
 for _name in _SUBMODULES:
     sys.modules[f"{__name__}.{_name}"] = importlib.import_module(f"muspace_b200.{_name}")
+for _name, _target in _RENAMED.items():
+    _module = importlib.import_module(f"muspace_b200.{_target}")
+    sys.modules[f"{__name__}.{_name}"] = _module
+    _parent, _, _leaf = _name.rpartition(".")
+    setattr(sys.modules[f"{__name__}.{_parent}"], _leaf, _module)
 ops = muspace_b200.ops
 runtime = muspace_b200.runtime
 patcher = importlib.import_module("muspace_b200.patcher")

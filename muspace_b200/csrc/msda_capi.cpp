@@ -15,6 +15,7 @@
 
 #include "../../include/muspace_msda.h"
 #include "deform_agg.h"
+#include "flash_sca.h"
 #include "msda_kernels.h"
 
 namespace {
@@ -543,6 +544,132 @@ int deformable_aggregation_backward_base(const DLTensor* mc_ms_feat, const DLTen
   return da_backward_entry(mc_ms_feat, spatial_shape, scale_start_index, sampling_location, weights, grad_output,
                            grad_mc_ms_feat, grad_sampling_location, grad_weights, stream, false,
                            "deformable_aggregation_backward_base");
+}
+
+// ---------------------------------------------------------------------------
+// FlashSCA (csrc/flashbev/flash_bevpool_sca_musa.mu:262-399)
+// ---------------------------------------------------------------------------
+namespace {
+
+struct FscaViews {
+  fsca::Dims dims;
+  fsca::Args args;
+  int device;
+};
+
+// The reference's checks (fp32 / int32, contiguous, value rank 4, heads and
+// grid positive, C % heads == 0) plus the shape agreements its Python layer
+// made (mu_space/ops/flashbev.py:560-640).
+FscaViews fsca_views(const DLTensor* value, const DLTensor* proj, const DLTensor* spatial, const DLTensor* start,
+                     const DLTensor* image_size, const DLTensor* offsets, const DLTensor* weights, int heads,
+                     int points, int gx, int gy, int gz, int value_stride_n) {
+  require(value != nullptr, "value is null");
+  const int dev = value->device.device_id;
+  check_tensor(value, "value", kDLFloat, 32, 4, dev);
+  check_tensor(proj, "projection_matrices", kDLFloat, 32, 4, dev);
+  check_tensor(spatial, "spatial_shapes", kDLInt, 32, 2, dev);
+  check_tensor(start, "level_start_index", kDLInt, 32, 1, dev);
+  check_tensor(image_size, "image_size", kDLInt, 32, 1, dev);
+  check_tensor(offsets, "sampling_offsets", kDLFloat, 32, 8, dev);
+  check_tensor(weights, "attention_weights", kDLFloat, 32, 7, dev);
+  require(heads > 0 && points > 0, "num_heads and num_points must be positive");
+  require(gx > 0 && gy > 0 && gz > 0, "grid sizes must be positive");
+  const int64_t batch = value->shape[0], cams = value->shape[1], stride = value->shape[2], channels = value->shape[3];
+  const int64_t levels = spatial->shape[0];
+  require(channels % heads == 0, "channels must be divisible by num_heads");
+  require(proj->shape[0] == batch && proj->shape[1] == cams && proj->shape[2] == 3 && proj->shape[3] == 4,
+          "projection_matrices must have shape [B,N,3,4]");
+  require(spatial->shape[1] == 2 && start->shape[0] == levels && image_size->shape[0] == 2,
+          "level_start_index/image_size shapes must be [levels]/[2]");
+  const int64_t want[8] = {batch, gy, gx, heads, levels, points, gz, 2};
+  for (int i = 0; i < 8; ++i) require(offsets->shape[i] == want[i], "sampling_offsets must have shape [B,gy,gx,heads,L,P,gz,2]");
+  for (int i = 0; i < 7; ++i) require(weights->shape[i] == want[i], "attention_weights must have shape [B,gy,gx,heads,L,P,gz]");
+  require(value_stride_n >= 1 && value_stride_n <= stride, "value_stride_n must be in [1, value.size(2)]");
+  require(levels <= fsca::kMaxLevels, "at most 16 levels");
+  require(cams * gz <= fsca::kMaxPairs, "num_cams * grid_z must be at most 64");
+  const int64_t kMax = std::numeric_limits<int32_t>::max();
+  require(cams * stride <= kMax && batch * gx * gy <= kMax && channels <= kMax, "a size exceeds the supported range");
+  FscaViews v{};
+  v.dims = fsca::Dims{static_cast<int>(batch), static_cast<int>(cams), static_cast<int>(stride),
+                      static_cast<int>(channels), static_cast<int>(levels), heads, points, gx, gy, gz};
+  v.args.value = static_cast<const float*>(data_of(value));
+  v.args.projection = static_cast<const float*>(data_of(proj));
+  v.args.shapes = static_cast<const int*>(data_of(spatial));
+  v.args.starts = static_cast<const int*>(data_of(start));
+  v.args.image_size = static_cast<const int*>(data_of(image_size));
+  v.args.offsets = static_cast<const float*>(data_of(offsets));
+  v.args.weights = static_cast<const float*>(data_of(weights));
+  v.device = dev;
+  return v;
+}
+
+void fsca_require_lanes(const FscaViews& v, bool backward) {
+  require(fsca::lanes_per_head(v.dims, v.args, backward) != 0,
+          "flash_bevpool_sca needs channels / num_heads = 4 * {1, 2, 4, 8, 16, 32} and 16-byte aligned tensors");
+}
+
+}  // namespace
+
+int flash_bevpool_sca_forward(const DLTensor* value, const DLTensor* projection_matrices, const DLTensor* spatial_shapes,
+                              const DLTensor* level_start_index, const DLTensor* image_size,
+                              const DLTensor* sampling_offsets, const DLTensor* attention_weights, DLTensor* out,
+                              int num_heads, int num_points, int grid_x, int grid_y, int grid_z, float voxel_size_x,
+                              float voxel_size_y, float voxel_size_z, float voxel_x_min, float voxel_y_min,
+                              float voxel_z_min, int value_stride_n, float epsilon, void* stream) {
+  return guarded([&] {
+    FscaViews v = fsca_views(value, projection_matrices, spatial_shapes, level_start_index, image_size,
+                             sampling_offsets, attention_weights, num_heads, num_points, grid_x, grid_y, grid_z,
+                             value_stride_n);
+    check_tensor(out, "out", kDLFloat, 32, 4, v.device);
+    require(out->shape[0] == value->shape[0] && out->shape[1] == grid_y && out->shape[2] == grid_x &&
+                out->shape[3] == value->shape[3],
+            "out must have shape [B, gy, gx, C]");
+    v.args.out = static_cast<float*>(data_of(out));
+    fsca_require_lanes(v, false);
+    DeviceGuard guard(v.device);
+    const fsca::Grid grid{voxel_size_x, voxel_size_y, voxel_size_z, voxel_x_min, voxel_y_min, voxel_z_min};
+    check_launch(fsca::forward(v.dims, grid, epsilon, v.args, static_cast<cudaStream_t>(stream)),
+                 "flash_bevpool_sca_forward");
+  });
+}
+
+int flash_bevpool_sca_backward(const DLTensor* out_grad, const DLTensor* value, const DLTensor* projection_matrices,
+                               const DLTensor* spatial_shapes, const DLTensor* level_start_index,
+                               const DLTensor* image_size, const DLTensor* roi_range,
+                               const DLTensor* sampling_offsets, const DLTensor* attention_weights,
+                               DLTensor* value_grad, DLTensor* sampling_offsets_grad,
+                               DLTensor* attention_weights_grad, int num_heads, int num_points, int grid_x,
+                               int grid_y, int grid_z, int value_stride_n, float epsilon, void* stream) {
+  return guarded([&] {
+    FscaViews v = fsca_views(value, projection_matrices, spatial_shapes, level_start_index, image_size,
+                             sampling_offsets, attention_weights, num_heads, num_points, grid_x, grid_y, grid_z,
+                             value_stride_n);
+    check_tensor(out_grad, "out_grad", kDLFloat, 32, 4, v.device);
+    check_tensor(roi_range, "roi_range", kDLFloat, 32, 1, v.device);
+    check_tensor(value_grad, "value_grad", kDLFloat, 32, 4, v.device);
+    check_tensor(sampling_offsets_grad, "sampling_offsets_grad", kDLFloat, 32, 8, v.device);
+    check_tensor(attention_weights_grad, "attention_weights_grad", kDLFloat, 32, 7, v.device);
+    require(roi_range->shape[0] == 6, "roi_range must have shape [6]");
+    require(out_grad->shape[0] == value->shape[0] && out_grad->shape[1] == grid_y && out_grad->shape[2] == grid_x &&
+                out_grad->shape[3] == value->shape[3],
+            "out_grad must have shape [B, gy, gx, C]");
+    for (int i = 0; i < 4; ++i) require(value_grad->shape[i] == value->shape[i], "value_grad must have the shape of value");
+    for (int i = 0; i < 8; ++i)
+      require(sampling_offsets_grad->shape[i] == sampling_offsets->shape[i],
+              "sampling_offsets_grad must have the shape of sampling_offsets");
+    for (int i = 0; i < 7; ++i)
+      require(attention_weights_grad->shape[i] == attention_weights->shape[i],
+              "attention_weights_grad must have the shape of attention_weights");
+    v.args.roi = static_cast<const float*>(data_of(roi_range));
+    v.args.grad_out = static_cast<const float*>(data_of(out_grad));
+    v.args.grad_value = static_cast<float*>(data_of(value_grad));
+    v.args.grad_offsets = static_cast<float*>(data_of(sampling_offsets_grad));
+    v.args.grad_weights = static_cast<float*>(data_of(attention_weights_grad));
+    fsca_require_lanes(v, true);
+    DeviceGuard guard(v.device);
+    check_launch(fsca::backward(v.dims, epsilon, v.args, static_cast<cudaStream_t>(stream)),
+                 "flash_bevpool_sca_backward");
+  });
 }
 
 const char* msda_last_error(void) { return g_last_error.c_str(); }

@@ -86,7 +86,8 @@ def _is_cuda_tensor(tensor: torch.Tensor) -> bool:
     return tensor.device.type == "cuda"
 
 
-_KERNEL_NAMES = {"multi_scale_deformable_attn": "MSDA", "deformable_aggregation": "deformable aggregation"}
+_KERNEL_NAMES = {"multi_scale_deformable_attn": "MSDA", "deformable_aggregation": "deformable aggregation",
+                 "flash_bevpool_sca": "FlashSCA"}
 
 
 def explain_dispatch(

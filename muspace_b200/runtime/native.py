@@ -103,7 +103,7 @@ def _stream_of(tensors) -> int:
     return 0
 
 
-# argument kinds of the DLPack entry points: "t" tensor, "i" int (the stream is appended)
+# argument kinds of the DLPack entry points: "t" tensor, "i" int, "f" float (the stream is appended)
 _SIGNATURES: dict[str, tuple[str, ...]] = {
     "ms_deform_attn_forward": ("t",) * 6 + ("i",),
     "ms_deform_attn_backward": ("t",) * 9 + ("i",),
@@ -112,6 +112,10 @@ _SIGNATURES: dict[str, tuple[str, ...]] = {
     "deformable_aggregation_forward_base": ("t",) * 6,
     "deformable_aggregation_backward_opt": ("t",) * 9,
     "deformable_aggregation_backward_base": ("t",) * 9,
+    # value .. out, num_heads, num_points, gx, gy, gz, voxel size xyz, voxel min xyz, value_stride_n, epsilon
+    "flash_bevpool_sca_forward": ("t",) * 8 + ("i",) * 5 + ("f",) * 6 + ("i", "f"),
+    # out_grad .. attention_weights_grad, num_heads, num_points, gx, gy, gz, value_stride_n, epsilon
+    "flash_bevpool_sca_backward": ("t",) * 12 + ("i",) * 6 + ("f",),
 }
 
 
@@ -142,9 +146,8 @@ class NativeModule:
             fn = symbol
         else:
             symbol.restype = ctypes.c_int
-            symbol.argtypes = [
-                ctypes.POINTER(DLTensor) if kind == "t" else ctypes.c_int for kind in signature
-            ] + [ctypes.c_void_p]
+            kinds = {"t": ctypes.POINTER(DLTensor), "i": ctypes.c_int, "f": ctypes.c_float}
+            symbol.argtypes = [kinds[kind] for kind in signature] + [ctypes.c_void_p]
             fn = self._tensor_call(name, symbol, signature)
         self._cache[name] = fn
         return fn
@@ -162,6 +165,8 @@ class NativeModule:
                     view = _View(arg)
                     views.append(view)
                     c_args.append(ctypes.byref(view.dl))
+                elif kind == "f":
+                    c_args.append(float(arg))
                 else:
                     c_args.append(int(arg))
             stream = _stream_of(args)

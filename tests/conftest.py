@@ -19,8 +19,8 @@ def pytest_configure(config):
 
 
 def golden_names() -> list[str]:
-    """The MSDA golden cases (the deformable-aggregation ones are da_*.npz)."""
-    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith("da_"))
+    """The MSDA golden cases (deformable aggregation: da_*.npz, FlashSCA: fsca_*.npz)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz") if not p.stem.startswith(("da_", "fsca_")))
 
 
 def load_golden(name: str) -> dict[str, np.ndarray]:

@@ -1,0 +1,172 @@
+"""FlashSCA (flash_bevpool_sca): the oracle pinned to the reference's own CPU
+path, the op's validation and the C-ABI (CPU), and the sm_100a kernels against
+the golden vectors and the oracle (GPU).
+
+Mirrors the reference's ``tests/ops/test_flashbev.py`` SCA part: forward and
+gradients (value, sampling offsets, attention weights) against the Python
+reference, non-finite feature values read as 0, cells that no camera sees
+(output 0), roi_range as an alternative to voxel_size / voxel_min, and the
+validation messages.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+from muspace_b200.ops import flash_bevpool_sca
+from muspace_b200.runtime import native
+from oracle.flash_sca import flash_sca_forward_backward
+
+GOLDEN = ("four_cams", "d32", "batch2_nonfinite")
+TENSORS = ("value", "projection_matrices", "spatial_shapes", "level_start_index", "image_size", "sampling_offsets",
+           "attention_weights")
+GRADS = ("grad_value", "grad_sampling_offsets", "grad_attention_weights")
+
+
+def _golden(name):
+    z = np.load(ROOT / "tests" / "golden" / f"fsca_{name}.npz")
+    g = {k: z[k] for k in z.files}
+    t = {k: torch.from_numpy(g[k]) for k in TENSORS + ("grad_output", "output") + GRADS}
+    grid = dict(grid_size=tuple(int(v) for v in g["grid_size"]), voxel_size=tuple(float(v) for v in g["voxel_size"]),
+                voxel_min=tuple(float(v) for v in g["voxel_min"]))
+    return t, grid
+
+
+def test_golden_manifest_matches_files():
+    manifest = json.loads((ROOT / "tests" / "golden" / "FSCA_MANIFEST.json").read_text())
+    assert sorted(manifest["cases"]) == sorted(GOLDEN)
+    for name, meta in manifest["cases"].items():
+        digest = hashlib.sha256((ROOT / "tests" / "golden" / f"fsca_{name}.npz").read_bytes()).hexdigest()
+        assert digest == meta["sha256"], name
+
+
+@pytest.mark.parametrize("name", GOLDEN)
+def test_oracle_matches_the_reference_golden_vectors(name):
+    t, grid = _golden(name)
+    out, *grads = flash_sca_forward_backward(*[t[k] for k in TENSORS], grid["grid_size"], grid["voxel_size"],
+                                             grid["voxel_min"], t["grad_output"])
+    torch.testing.assert_close(out, t["output"], rtol=1e-5, atol=1e-5)
+    for got, key in zip(grads, GRADS):
+        torch.testing.assert_close(got, t[key], rtol=1e-5, atol=2e-5)
+
+
+def test_golden_cases_cover_unseen_cells_and_nonfinite_values():
+    t, _ = _golden("batch2_nonfinite")
+    assert not torch.isfinite(t["value"]).all()
+    cells = t["output"].abs().sum(-1)
+    assert (cells == 0).any() and (cells > 0).any()
+
+
+def test_validation_mirrors_the_reference():
+    t, grid = _golden("four_cams")
+    args = [t[k] for k in TENSORS]
+    bad = list(args)
+    bad[2] = bad[2].long()
+    with pytest.raises(TypeError, match="spatial_shapes must use int32"):
+        flash_bevpool_sca(*bad, **grid)
+    bad = list(args)
+    bad[5] = bad[5][..., :1].contiguous()
+    with pytest.raises(ValueError, match="invalid FlashSCA input ranks|sampling_offsets must have shape"):
+        flash_bevpool_sca(*bad, **grid)
+    with pytest.raises(ValueError, match="pass either roi_range or voxel_size/voxel_min"):
+        flash_bevpool_sca(*args, **grid, roi_range=[0, 1, 0, 1, 0, 1])
+    with pytest.raises(ValueError, match="value_stride_n must be in"):
+        flash_bevpool_sca(*args, **grid, value_stride_n=10_000)
+    with pytest.raises(RuntimeError, match="FlashSCA kernels need CUDA tensors"):
+        flash_bevpool_sca(*args, **grid)
+
+
+def test_c_abi_refuses_cpu_tensors_and_wrong_arity():
+    t, grid = _golden("four_cams")
+    out = torch.zeros(1, 4, 4, 8)
+    fwd = native.native_function("flash_bevpool_sca_forward")
+    with pytest.raises(RuntimeError, match="value must be a CUDA tensor"):
+        fwd(*[t[k] for k in TENSORS], out, 2, 2, 4, 4, 2, 2.5, 2.5, 2.0, -5.0, -5.0, -1.0, t["value"].shape[2], 1e-5)
+    with pytest.raises(TypeError, match="takes 19 arguments"):
+        native.native_function("flash_bevpool_sca_backward")(out)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------------------
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", GOLDEN)
+def test_op_matches_the_reference_golden_vectors(cuda_device, name):
+    t, grid = _golden(name)
+    dev = {k: t[k].to(cuda_device) for k in TENSORS}
+    for k in ("value", "sampling_offsets", "attention_weights"):
+        dev[k].requires_grad_(True)
+    out = flash_bevpool_sca(*[dev[k] for k in TENSORS], **grid)
+    out.backward(t["grad_output"].to(cuda_device))
+    torch.testing.assert_close(out.detach().cpu(), t["output"], rtol=1e-4, atol=1e-4)
+    for key, leaf in zip(GRADS, ("value", "sampling_offsets", "attention_weights")):
+        torch.testing.assert_close(dev[leaf].grad.cpu(), t[key], rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+def test_roi_range_equals_voxel_size_and_min(cuda_device):
+    t, grid = _golden("four_cams")
+    dev = [t[k].to(cuda_device) for k in TENSORS]
+    gx, gy, gz = grid["grid_size"]
+    (sx, sy, sz), (x0, y0, z0) = grid["voxel_size"], grid["voxel_min"]
+    roi = [x0, x0 + gx * sx, y0, y0 + gy * sy, z0, z0 + gz * sz]
+    a = flash_bevpool_sca(*dev, **grid)
+    b = flash_bevpool_sca(*dev, grid["grid_size"], roi_range=roi)
+    torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
+
+
+def _cameras(batch, cams, image_hw, gen, height=1.5):
+    img_h, img_w = image_hw
+    mats = torch.zeros(batch, cams, 3, 4)
+    for b in range(batch):
+        for c in range(cams):
+            yaw = 2 * math.pi * c / cams + float(torch.randn((), generator=gen)) * 0.05
+            rot = torch.tensor([[math.sin(yaw), -math.cos(yaw), 0.0], [0.0, 0.0, -1.0],
+                                [math.cos(yaw), math.sin(yaw), 0.0]])
+            k = torch.tensor([[img_w * 0.5, 0.0, img_w * 0.5], [0.0, img_h * 0.5, img_h * 0.5], [0.0, 0.0, 1.0]])
+            mats[b, c, :, :3] = k @ rot
+            mats[b, c, :, 3] = k @ (-(rot @ torch.tensor([0.0, 0.0, height])))
+    return mats
+
+
+def bevformer_inputs(device, *, batch=1, cams=6, grid=(50, 50, 4), channels=256, heads=8, points=4, seed=5):
+    g = torch.Generator().manual_seed(seed)
+    image_hw = (480, 800)
+    shapes = [(60, 100), (30, 50), (15, 25), (8, 13)]
+    sizes = [h * w for h, w in shapes]
+    value = torch.randn(batch, cams, sum(sizes), channels, generator=g)
+    proj = _cameras(batch, cams, image_hw, g)
+    gx, gy, gz = grid
+    offsets = torch.randn(batch, gy, gx, heads, len(shapes), points, gz, 2, generator=g) * 2.0
+    weights = torch.rand(batch, gy, gx, heads, len(shapes), points, gz, generator=g) / (len(shapes) * points * gz)
+    t = [value, proj, torch.tensor(shapes, dtype=torch.int32),
+         torch.tensor([sum(sizes[:i]) for i in range(len(shapes))], dtype=torch.int32),
+         torch.tensor(image_hw, dtype=torch.int32), offsets, weights]
+    kw = dict(grid_size=grid, voxel_size=(102.4 / gx, 102.4 / gy, 8.0 / gz), voxel_min=(-51.2, -51.2, -5.0))
+    return [x.to(device) for x in t], kw
+
+
+@pytest.mark.gpu
+def test_bevformer_like_case_matches_the_oracle(cuda_device):
+    t, kw = bevformer_inputs(cuda_device, grid=(24, 24, 4))
+    leaves = list(t)
+    for i in (0, 5, 6):
+        leaves[i] = t[i].clone().requires_grad_(True)
+    out = flash_bevpool_sca(*leaves, **kw)
+    grad = torch.randn(out.shape, generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    out.backward(grad)
+    exp = flash_sca_forward_backward(*[x.cpu() for x in t], kw["grid_size"], kw["voxel_size"], kw["voxel_min"],
+                                     grad.cpu())
+    assert out.abs().sum() > 0
+    torch.testing.assert_close(out.detach().cpu(), exp[0], rtol=1e-4, atol=1e-4)
+    for leaf, ref in zip((leaves[0], leaves[5], leaves[6]), exp[1:]):
+        torch.testing.assert_close(leaf.grad.cpu(), ref, rtol=1e-3, atol=1e-3)
