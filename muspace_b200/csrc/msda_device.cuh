@@ -99,11 +99,16 @@ struct Words {
 template <int kBytes>
 __device__ __forceinline__ Words<kBytes / 4> ldg_words(const void* p) {
   Words<kBytes / 4> r;
-  if constexpr (kBytes == 16) {
+  if constexpr (kBytes == 32) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    r.w[0] = a.x, r.w[1] = a.y, r.w[2] = a.z, r.w[3] = a.w;
+    r.w[4] = b.x, r.w[5] = b.y, r.w[6] = b.z, r.w[7] = b.w;
+  } else if constexpr (kBytes == 16) {
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
     r.w[0] = v.x, r.w[1] = v.y, r.w[2] = v.z, r.w[3] = v.w;
   } else {
-    static_assert(kBytes == 8, "lane slices are 8 or 16 bytes");
+    static_assert(kBytes == 8, "lane slices are 8, 16 or 32 bytes");
     const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
     r.w[0] = v.x, r.w[1] = v.y;
   }
@@ -191,9 +196,11 @@ __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
 }
 
 // Vector reduction into fp32 global memory (no return value -> RED, not ATOM).
+// No "memory" clobber: the kernels never read the gradient buffers they
+// reduce into, so loads of other tensors may move across a RED (the compiler
+// can then keep several samples' corner gathers in flight).
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 
 // ---------------------------------------------------------------------------

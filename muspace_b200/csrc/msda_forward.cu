@@ -29,39 +29,59 @@ namespace msda {
 #ifndef MSDA_FWD_PACKED
 #define MSDA_FWD_PACKED 1
 #endif
+// CTAs per SM the forward's register budget is sized for: the gathers are
+// latency-bound, so occupancy (4 x 256 threads at <= 64 registers) pays.
+#ifndef MSDA_FWD_MINBLOCKS
+#define MSDA_FWD_MINBLOCKS 4
+#endif
+// Samples of a chunk whose corner gathers are issued together (the loads of
+// the unrolled samples are in flight at once).
+#ifndef MSDA_FWD_UNROLL
+#define MSDA_FWD_UNROLL 1
+#endif
+constexpr int kFwdUnroll = MSDA_FWD_UNROLL;
 
-// Staging slots of the forward kernels: C = min(G, 8) samples per chunk plus
-// one slot of padding per group, so the groups of a warp reading slot i at
-// once hit different shared-memory banks.
-template <int G>
-struct FwdSlots {
-  static constexpr int kSamples = Chunk<G, 8>::kSamples;
-  static constexpr int kStride = Chunk<G, 8>::kStagerStride;
+// Samples staged per chunk by the forward kernels (lane sub stages samples
+// sub, sub + G, ... of the chunk), and their shared slots: one per sample plus
+// one of padding per group, so the groups of a warp reading slot i at once hit
+// different shared-memory banks.
+#ifndef MSDA_FWD_CHUNK
+#define MSDA_FWD_CHUNK 8
+#endif
+template <int G, int kChunk = MSDA_FWD_CHUNK>
+struct FwdSlots {  // 1-lane groups (256 per CTA) stage 4 samples so the slots fit 48 KB
+  static constexpr int kSamples = kChunk < 4 * G ? kChunk : 4 * G;
   static constexpr int kPerGroup = kSamples + 1;
-  static constexpr int kTotal = (kCtaThreads / G) * kPerGroup;
 };
+
+// Lane bytes of the forward for bf16 / fp32 storage (16: one 16-byte load per
+// corner; 32: two, half the lanes per head-row).
+#ifndef MSDA_FWD_LANE_BYTES_BF16
+#define MSDA_FWD_LANE_BYTES_BF16 16
+#endif
+#ifndef MSDA_FWD_LANE_BYTES_F32
+#define MSDA_FWD_LANE_BYTES_F32 16
+#endif
 
 // acc (this lane's channel pairs) += sum over the head-row's samples of
 // sum_k (w_k a) v_k. vbase points at the lane's channel slice of pixel 0 of
 // the head's value map; lp / wp at the head-row's locations / weights; row /
 // wa at the group's staging slots. Every lane of the warp must call it (it
 // syncs the warp), live = false for a lane group without an item.
-template <typename T, int G>
+template <typename T, int G, int kBytes, int kChunk = MSDA_FWD_CHUNK>
 __device__ __forceinline__ void gather_head_row(const Level* levels, int points, int samples, bool live,
                                                 const T* vbase, int row_stride, const T* lp, const T* wp, int sub,
-                                                int4* row, float4* wa, float2 (&acc)[Slice<T, 16>::kPairs]) {
-  using S = Slice<T, 16>;
-  constexpr int kPairs = S::kPairs, kWords = 4;
-  constexpr int C = FwdSlots<G>::kSamples, kOwn = FwdSlots<G>::kStride;
+                                                int4* row, float4* wa, float2 (&acc)[Slice<T, kBytes>::kPairs]) {
+  using S = Slice<T, kBytes>;
+  constexpr int kPairs = S::kPairs, kWords = kBytes / 4;
+  constexpr int C = FwdSlots<G, kChunk>::kSamples;
 #pragma unroll
   for (int i = 0; i < kPairs; ++i) acc[i] = make_float2(0.0f, 0.0f);
   for (int s0 = 0; s0 < samples; s0 += C) {
-    if (sub % kOwn == 0) {
-      const int i = sub / kOwn;
-      stage_sample(levels, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
-    }
-    __syncwarp();
 #pragma unroll
+    for (int i = sub; i < C; i += G) stage_sample(levels, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
+    __syncwarp();
+#pragma unroll kFwdUnroll
     for (int i = 0; i < C; ++i) {
       const int4 r4 = row[i];
       const float4 w4 = wa[i];
@@ -70,7 +90,7 @@ __device__ __forceinline__ void gather_head_row(const Level* levels, int points,
       Words<kWords> raw[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        raw[k] = rows[k] >= 0 ? ldg_words<16>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
+        raw[k] = rows[k] >= 0 ? ldg_words<kBytes>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
                               : zero_words<kWords>();
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -92,22 +112,34 @@ __device__ __forceinline__ void gather_head_row(const Level* levels, int points,
   }
 }
 
-template <typename T, int G>
-__global__ void __launch_bounds__(kCtaThreads) forward_vec_kernel(Dims d, const T* __restrict__ value,
-                                                               const int64_t* __restrict__ shapes,
-                                                               const int64_t* __restrict__ starts,
-                                                               const T* __restrict__ loc, const T* __restrict__ weight,
-                                                               T* __restrict__ out, const int* __restrict__ order) {
-  using S = Slice<T, 16>;
+// Stores / loads a lane's kBytes slice of channels as fp32 pairs.
+template <typename T, int kBytes>
+__device__ __forceinline__ void store_slice(T* dst, const float2 (&acc)[Slice<T, kBytes>::kPairs]) {
+  constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16 bytes
+#pragma unroll
+  for (int h = 0; h < kBytes / 16; ++h) {
+    float f[kPer16];
+#pragma unroll
+    for (int q = 0; q < kPer16 / 2; ++q) f[2 * q] = acc[h * kPer16 / 2 + q].x, f[2 * q + 1] = acc[h * kPer16 / 2 + q].y;
+    st16(dst + h * kPer16, Vec16<T>::pack(f));
+  }
+}
+
+template <typename T, int G, int kBytes, int kChunk>
+__global__ void __launch_bounds__(kCtaThreads, MSDA_FWD_MINBLOCKS) forward_vec_kernel(
+    Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
+    const T* __restrict__ loc, const T* __restrict__ weight, T* __restrict__ out, const int* __restrict__ order) {
+  using S = Slice<T, kBytes>;
   constexpr int kCh = S::kChannels, kPairs = S::kPairs;
+  constexpr int kGroups = kCtaThreads / G;
+  using Slots = FwdSlots<G, kChunk>;
   extern __shared__ Level levels[];
-  __shared__ int4 s_row[FwdSlots<G>::kTotal];
-  __shared__ float4 s_wa[FwdSlots<G>::kTotal];
+  __shared__ int4 s_row[kGroups * Slots::kPerGroup];
+  __shared__ float4 s_wa[kGroups * Slots::kPerGroup];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
-  const int base = (threadIdx.x / G) * FwdSlots<G>::kPerGroup;
-  constexpr int kGroups = kCtaThreads / G;
+  const int base = (threadIdx.x / G) * Slots::kPerGroup;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int row_stride = d.heads * d.channels;  // elements between neighbouring pixels
   const int samples = d.levels * d.points;
@@ -123,14 +155,9 @@ __global__ void __launch_bounds__(kCtaThreads) forward_vec_kernel(Dims d, const 
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
     const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     float2 acc[kPairs];
-    gather_head_row<T, G>(levels, d.points, samples, live, vbase, row_stride, loc + item * samples * 2,
-                          weight + item * samples, sub, s_row + base, s_wa + base, acc);
-    if (live) {
-      float f[kCh];
-#pragma unroll
-      for (int q = 0; q < kPairs; ++q) f[2 * q] = acc[q].x, f[2 * q + 1] = acc[q].y;
-      st16(out + item * d.channels + sub * kCh, Vec16<T>::pack(f));
-    }
+    gather_head_row<T, G, kBytes, kChunk>(levels, d.points, samples, live, vbase, row_stride, loc + item * samples * 2,
+                                  weight + item * samples, sub, s_row + base, s_wa + base, acc);
+    if (live) store_slice<T, kBytes>(out + item * d.channels + sub * kCh, acc);
   }
 }
 
@@ -149,14 +176,14 @@ __global__ void __launch_bounds__(kCtaThreads) scatter_div_vec_kernel(
     const int64_t* __restrict__ index, const T* __restrict__ count, T* __restrict__ slots) {
   using S = Slice<T, 16>;
   constexpr int kCh = S::kChannels, kPairs = S::kPairs;
+  constexpr int kGroups = kCtaThreads / G;
   extern __shared__ Level levels[];
-  __shared__ int4 s_row[FwdSlots<G>::kTotal];
-  __shared__ float4 s_wa[FwdSlots<G>::kTotal];
+  __shared__ int4 s_row[kGroups * FwdSlots<G>::kPerGroup];
+  __shared__ float4 s_wa[kGroups * FwdSlots<G>::kPerGroup];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
   const int base = (threadIdx.x / G) * FwdSlots<G>::kPerGroup;
-  constexpr int kGroups = kCtaThreads / G;
   const int64_t items = static_cast<int64_t>(sd.batch) * sd.valid_len * d.heads;
   const int row_stride = d.heads * d.channels;
   const int samples = d.levels * d.points;
@@ -174,7 +201,7 @@ __global__ void __launch_bounds__(kCtaThreads) scatter_div_vec_kernel(
     const int64_t lrow = (image * d.queries + q) * d.heads + h;  // rebatched (image, q, h) row
     const T* vbase = value + (image * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     float2 acc[kPairs];
-    gather_head_row<T, G>(levels, d.points, samples, live, vbase, row_stride, loc + lrow * samples * 2,
+    gather_head_row<T, G, 16>(levels, d.points, samples, live, vbase, row_stride, loc + lrow * samples * 2,
                           weight + lrow * samples, sub, s_row + base, s_wa + base, acc);
     const int64_t bev = index[q];
     if (live && bev >= 0 && bev < sd.num_query) {
@@ -234,30 +261,41 @@ __global__ void __launch_bounds__(256) forward_scalar_kernel(Dims d, const T* __
   }
 }
 
-template <typename T, int G>
+template <typename T, int G, int kBytes>
 static cudaError_t launch_forward_vec(const Dims& d, const Args& a, cudaStream_t stream) {
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int64_t groups_per_cta = kCtaThreads / G;
   const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
-  forward_vec_kernel<T, G><<<grid, kCtaThreads, level_smem(d), stream>>>(
+  // head-rows of at most 4 samples (single-level cases) stage 4 at a time
+  auto kernel = d.levels * d.points <= 4 ? forward_vec_kernel<T, G, kBytes, 4>
+                                         : forward_vec_kernel<T, G, kBytes, MSDA_FWD_CHUNK>;
+  kernel<<<grid, kCtaThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<T*>(a.out), a.order);
   return cudaGetLastError();
 }
 
+template <typename T, int kBytes>
+static cudaError_t launch_forward_lanes(int g, const Dims& d, const Args& a, cudaStream_t stream) {
+  switch (g) {
+    case 1: return launch_forward_vec<T, 1, kBytes>(d, a, stream);
+    case 2: return launch_forward_vec<T, 2, kBytes>(d, a, stream);
+    case 4: return launch_forward_vec<T, 4, kBytes>(d, a, stream);
+    case 8: return launch_forward_vec<T, 8, kBytes>(d, a, stream);
+    case 16: return launch_forward_vec<T, 16, kBytes>(d, a, stream);
+    case 32: return launch_forward_vec<T, 32, kBytes>(d, a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <typename T>
 static cudaError_t launch_forward_t(const Dims& d, const Args& a, cudaStream_t stream) {
-  const int g = vec_group(d.channels, sizeof(T), a);
-  switch (g) {
-    case 1: return launch_forward_vec<T, 1>(d, a, stream);
-    case 2: return launch_forward_vec<T, 2>(d, a, stream);
-    case 4: return launch_forward_vec<T, 4>(d, a, stream);
-    case 8: return launch_forward_vec<T, 8>(d, a, stream);
-    case 16: return launch_forward_vec<T, 16>(d, a, stream);
-    case 32: return launch_forward_vec<T, 32>(d, a, stream);
-    default: break;
+  constexpr int kWide = sizeof(T) == 2 ? MSDA_FWD_LANE_BYTES_BF16 : MSDA_FWD_LANE_BYTES_F32;
+  if constexpr (kWide == 32) {
+    if (const int g = vec_lanes(d.channels, sizeof(T), 32, a)) return launch_forward_lanes<T, 32>(g, d, a, stream);
   }
+  if (const int g = vec_group(d.channels, sizeof(T), a)) return launch_forward_lanes<T, 16>(g, d, a, stream);
   const int64_t total = static_cast<int64_t>(d.batch) * d.queries * d.heads * d.channels;
   const int64_t blocks = (total + kCtaThreads - 1) / kCtaThreads;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
