@@ -49,6 +49,9 @@ namespace msda {
 #ifndef MSDA_BWD_MINBLOCKS_BF16
 #define MSDA_BWD_MINBLOCKS_BF16 3
 #endif
+#ifndef MSDA_BWD_PAIR
+#define MSDA_BWD_PAIR 1
+#endif
 #ifndef MSDA_BWD_DEDUP
 #define MSDA_BWD_DEDUP 1
 #endif
@@ -236,6 +239,179 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
   }
 }
 
+// Backward with the work of a sample split two ways. kCPL = 16-byte chunks of
+// the head-row each lane of a pair holds (the row has 2 kCPL chunks), and
+// G = D / 4 lanes per head-row (each owning a 4-channel fp32 slice of the
+// gradients). Per chunk of Cs staged samples:
+//  - stage / fold as in backward_vec_kernel;
+//  - dots: a lane pair owns a sample, lane h of the pair holding chunks h,
+//    h + 2, ... (so the pair's first loads fill whole 32-byte sectors); it
+//    gathers those chunks of the four corners, forms the corner dots with its
+//    grad_output chunks, one xor shuffle completes them, and lane 0 of the pair
+//    writes grad_w / grad_loc: no transpose reduction, no geometry per lane;
+//  - REDs: every lane sends its 4-channel slice of (sum of w_k a) * g for each
+//    first-occurrence corner row (whole 128-byte lines per group for D = 32).
+template <typename T, int kCPL>
+struct PairShape {
+  static constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte chunk
+  static constexpr int kChannels = 2 * kCPL * kPer16;              // D
+  static constexpr int G = kChannels / 4;                          // lanes per head-row
+  static constexpr int kPairs16 = kPer16 / 2;                      // fp32 pairs per chunk
+#ifndef MSDA_PAIR_CORNERS
+#define MSDA_PAIR_CORNERS 2
+#endif
+  // corner gathers issued together (register budget: kCPL * 4 words each)
+  static constexpr int kCornersInFlight = kCPL == 1 ? 4 : (kCPL == 2 ? MSDA_PAIR_CORNERS : 1);
+};
+
+template <typename T, int kCPL, int kStageMax, bool kScatter>
+__global__ void __launch_bounds__(kCtaThreads, 3) backward_pair_kernel(
+    Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
+    const T* __restrict__ loc, const T* __restrict__ weight, const T* __restrict__ grad_out,
+    float* __restrict__ grad_value, float* __restrict__ grad_loc, float* __restrict__ grad_weight,
+    const int* __restrict__ order) {
+  using Sh = PairShape<T, kCPL>;
+  using S16 = Slice<T, 16>;
+  constexpr int G = Sh::G;
+  constexpr int Cs = G < kStageMax ? G : kStageMax;  // samples staged per chunk
+  constexpr int kStage = G / Cs;                     // stager lanes: sub % kStage == 0
+  constexpr int kPerPass = G / 2;                     // samples whose dots run at once
+  constexpr int kPasses = Cs / kPerPass > 0 ? Cs / kPerPass : 1;
+  constexpr int kGroups = kCtaThreads / G;
+  constexpr int kSlots = Cs + 1;
+  extern __shared__ Level levels[];
+  __shared__ int4 s_row[kGroups * kSlots];
+  __shared__ float4 s_wa[kGroups * kSlots];
+  __shared__ float4 s_geo[kGroups * kSlots];
+  stage_levels(levels, shapes, starts, d);
+
+  const int sub = threadIdx.x % G;
+  const int half = sub & 1, member = sub >> 1;  // lane of the pair, pair within the group
+  const int base = (threadIdx.x / G) * kSlots;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int row_stride = d.heads * d.channels;
+  const int samples = d.levels * d.points;
+
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kGroups;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * kGroups + threadIdx.x / G;
+       item - (threadIdx.x % 32) / G < items; item += stride) {
+    const bool live = item < items;
+    const int64_t slot = live ? item : items - 1;
+    const int64_t it = order ? order[slot] : slot;
+    const int h = static_cast<int>(it % d.heads);
+    const int64_t b = it / (static_cast<int64_t>(d.queries) * d.heads);
+    const int64_t head0 = (b * d.spatial_size) * row_stride + h * d.channels;
+    const T* vrow = value + head0;
+    float* gbase = grad_value + head0 + sub * 4;
+    const T* lp = loc + it * samples * 2;
+    const T* wp = weight + it * samples;
+    const T* grow = grad_out + it * d.channels;
+
+    // grad_output in the pair layout (chunks half, half + 2, ...) and as this
+    // lane's 4-channel slice for the REDs
+    float2 ga[kCPL][Sh::kPairs16];
+    {
+      const uint64_t policy = evict_first_policy();
+#pragma unroll
+      for (int j = 0; j < kCPL; ++j) {
+        const Words<4> w = ld_stream_words<16>(grow + (2 * j + half) * Sh::kPer16, policy);
+#pragma unroll
+        for (int q = 0; q < Sh::kPairs16; ++q) ga[j][q] = S16::pair(w, q);
+      }
+    }
+    float2 gr[2];
+    {
+      const Words<4 * static_cast<int>(sizeof(T)) / 4> w =
+          ld_stream_words<4 * static_cast<int>(sizeof(T))>(grow + 4 * sub, evict_first_policy());
+      gr[0] = Slice<T, 4 * sizeof(T)>::pair(w, 0);
+      gr[1] = Slice<T, 4 * sizeof(T)>::pair(w, 1);
+    }
+
+    for (int s0 = 0; s0 < samples; s0 += Cs) {
+      if (sub % kStage == 0) {
+        const int i = sub / kStage;
+        float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo);
+        s_geo[base + i] = geo;
+      }
+      __syncwarp();
+#if MSDA_BWD_DEDUP
+      if constexpr (kScatter)
+        fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(s_row + base),
+                                      reinterpret_cast<float*>(s_wa + base), sub);
+#endif
+#pragma unroll 1
+      for (int p = 0; p < kPasses; ++p) {
+        // dots of sample i by the pair
+        const int i = p * kPerPass + member;
+        if (i < Cs) {
+          const int4 r4 = s_row[base + i];
+          const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+          float t[4];
+#pragma unroll
+          for (int k0 = 0; k0 < 4; k0 += Sh::kCornersInFlight) {
+            Words<4> raw[Sh::kCornersInFlight][kCPL];
+#pragma unroll
+            for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
+              const int row = rows[k0 + kk];
+#pragma unroll
+              for (int j = 0; j < kCPL; ++j)
+                raw[kk][j] = row >= 0 ? ldg_words<16>(vrow + static_cast<int64_t>(row) * row_stride +
+                                                      (2 * j + half) * Sh::kPer16)
+                                      : zero_words<4>();
+            }
+#pragma unroll
+            for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
+              float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+              for (int j = 0; j < kCPL; ++j)
+#pragma unroll
+                for (int q = 0; q < Sh::kPairs16; ++q) acc = ffma2(ga[j][q], S16::pair(raw[kk][j], q), acc);
+              t[k0 + kk] = acc.x + acc.y;
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], 1);
+          const int s = s0 + i;
+          if (half == 0 && live && s < samples) {
+            const float4 geo = s_geo[base + i];
+            float gw = 0.0f, gx = 0.0f, gy = 0.0f;
+            if (geo.w != 0.0f) {
+              const Level lv = levels[s / d.points];
+              const float lh = geo.x, lw = geo.y, a = geo.z;
+              const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
+              gw = __fmul_rn(hh, hw) * t[0] + __fmul_rn(hh, lw) * t[1] + __fmul_rn(lh, hw) * t[2] +
+                   __fmul_rn(lh, lw) * t[3];
+              gx = static_cast<float>(lv.width) * a * (hh * (t[1] - t[0]) + lh * (t[3] - t[2]));
+              gy = static_cast<float>(lv.height) * a * (hw * (t[2] - t[0]) + lw * (t[3] - t[1]));
+            }
+            const int64_t so = it * samples + s;
+            grad_weight[so] = gw;
+            *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(gx, gy);
+          }
+        }
+        // REDs of the same samples by every lane's slice
+        if constexpr (kScatter) {
+#pragma unroll
+          for (int m = 0; m < kPerPass; ++m) {
+            const int i2 = p * kPerPass + m;
+            if (i2 >= Cs) break;
+            const int4 r4 = s_row[base + i2];
+            const float4 w4 = s_wa[base + i2];
+            const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+            const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (rows[k] >= 0 && wa[k] != 0.0f)
+                scatter_slice<2>(gbase + static_cast<int64_t>(rows[k]) * row_stride, wa[k], gr);
+          }
+        }
+      }
+      __syncwarp();  // the next chunk's staging overwrites the slots read above
+    }
+  }
+}
+
 // Any D: one thread per head-row, channels in a loop (no cross-thread
 // reduction needed); grad_value through scalar fp32 atomics.
 template <typename T>
@@ -324,8 +500,44 @@ static cudaError_t launch_backward_lanes(int g, const Dims& d, const Args& a, cu
   }
 }
 
+template <typename T, int kCPL>
+static cudaError_t launch_backward_pair(const Dims& d, const Args& a, cudaStream_t stream) {
+  constexpr int G = PairShape<T, kCPL>::G;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int64_t groups_per_cta = kCtaThreads / G;
+  const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
+  const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
+  const bool short_rows = d.levels * d.points <= 4;
+  auto kernel = short_rows ? (a.skip_grad_value ? backward_pair_kernel<T, kCPL, 4, false>
+                                                : backward_pair_kernel<T, kCPL, 4, true>)
+                           : (a.skip_grad_value ? backward_pair_kernel<T, kCPL, 8, false>
+                                                : backward_pair_kernel<T, kCPL, 8, true>);
+  kernel<<<grid, kCtaThreads, level_smem(d), stream>>>(
+      d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
+      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight,
+      a.order);
+  return cudaGetLastError();
+}
+
 template <typename T>
 static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t stream) {
+#if MSDA_BWD_PAIR
+  // The lane-pair kernel where it measured faster on B200: bf16 rows of 2 or 4
+  // chunks of 16 bytes (D = 16, 32) with more than 4 samples per head-row
+  // (c2 / c4: backward 1.18 -> 1.11 ms / 9.38 -> 8.81 ms). fp32 rows (4
+  // chunks per lane, one corner in flight) and single-level rows ran slower
+  // than backward_vec_kernel.
+  if constexpr (sizeof(T) == 2) {
+    if (d.levels * d.points > 4 && vec_lanes(d.channels, sizeof(T), 16, a) != 0 &&
+        vec_lanes(d.channels, 4, 16, a) != 0) {
+      switch (d.channels * static_cast<int>(sizeof(T)) / 32) {
+        case 1: return launch_backward_pair<T, 1>(d, a, stream);
+        case 2: return launch_backward_pair<T, 2>(d, a, stream);
+        default: break;
+      }
+    }
+  }
+#endif
   // bf16: 8-byte lanes (4 channels, whole-line REDs) up to D = 128, 16-byte
   // lanes for D = 256; fp32: 16-byte lanes (4 channels).
   if constexpr (sizeof(T) == 2) {
