@@ -52,6 +52,9 @@ namespace msda {
 #ifndef MSDA_BWD_PAIR
 #define MSDA_BWD_PAIR 1
 #endif
+#ifndef MSDA_BWD_MIXED_FMA
+#define MSDA_BWD_MIXED_FMA 1
+#endif
 #ifndef MSDA_BWD_DEDUP
 #define MSDA_BWD_DEDUP 1
 #endif
@@ -309,14 +312,19 @@ __global__ void __launch_bounds__(kCtaThreads, 3) backward_pair_kernel(
 
     // grad_output in the pair layout (chunks half, half + 2, ...) and as this
     // lane's 4-channel slice for the REDs
+    // bf16 with the mixed-precision FMA keeps grad_output as raw words
+    constexpr bool kMixed = sizeof(T) == 2 && MSDA_BWD_MIXED_FMA;
     float2 ga[kCPL][Sh::kPairs16];
+    Words<4> graw[kCPL];
     {
       const uint64_t policy = evict_first_policy();
 #pragma unroll
       for (int j = 0; j < kCPL; ++j) {
-        const Words<4> w = ld_stream_words<16>(grow + (2 * j + half) * Sh::kPer16, policy);
+        graw[j] = ld_stream_words<16>(grow + (2 * j + half) * Sh::kPer16, policy);
+        if constexpr (!kMixed) {
 #pragma unroll
-        for (int q = 0; q < Sh::kPairs16; ++q) ga[j][q] = S16::pair(w, q);
+          for (int q = 0; q < Sh::kPairs16; ++q) ga[j][q] = S16::pair(graw[j], q);
+        }
       }
     }
     float2 gr[2];
@@ -364,9 +372,15 @@ __global__ void __launch_bounds__(kCtaThreads, 3) backward_pair_kernel(
             for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
               float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-              for (int j = 0; j < kCPL; ++j)
+              for (int j = 0; j < kCPL; ++j) {
+                if constexpr (kMixed) {
 #pragma unroll
-                for (int q = 0; q < Sh::kPairs16; ++q) acc = ffma2(ga[j][q], S16::pair(raw[kk][j], q), acc);
+                  for (int q = 0; q < 4; ++q) acc = fma_bf16x2_f32(graw[j].w[q], raw[kk][j].w[q], acc);
+                } else {
+#pragma unroll
+                  for (int q = 0; q < Sh::kPairs16; ++q) acc = ffma2(ga[j][q], S16::pair(raw[kk][j], q), acc);
+                }
+              }
               t[k0 + kk] = acc.x + acc.y;
             }
           }

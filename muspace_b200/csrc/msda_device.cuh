@@ -190,6 +190,17 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.u) : "l"(x.u), "l"(y.u), "l"(z.u));
   return r.f;
 }
+// acc.x += lo(g) * lo(v), acc.y += hi(g) * hi(v) for two words of two bf16
+// channels each, in fp32 (sm_100 mixed-precision FMA: the bf16 x bf16 product
+// is exact in fp32, so this equals unpacking both words and using fmaf).
+__device__ __forceinline__ float2 fma_bf16x2_f32(uint32_t g, uint32_t v, float2 acc) {
+  asm("{\n .reg .b16 gl, gh, vl, vh;\n mov.b32 {gl, gh}, %2;\n mov.b32 {vl, vh}, %3;\n"
+      " fma.rn.f32.bf16 %0, gl, vl, %0;\n fma.rn.f32.bf16 %1, gh, vh, %1;\n}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "r"(g), "r"(v));
+  return acc;
+}
+
 // A 32-bit word of two bf16 channels as (low channel, high channel) in fp32.
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
