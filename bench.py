@@ -60,6 +60,8 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--quiet", action="store_true", help="print only the JSON line")
+    p.add_argument("--op", choices=("msda", "deformable_aggregation", "flash_sca", "sca_scatter"), default="msda",
+                   help="msda (default: the headline workload) or one of the ops built next to it")
     return p.parse_args()
 
 
@@ -485,6 +487,216 @@ def run_query_variant(args, cfg, dtype, rank, world, device):
     }
 
 
+# --------------------------------------------------------------------------------------
+# the ops next to MSDA (--op): one JSON line each, same contract as the headline
+# --------------------------------------------------------------------------------------
+
+
+def _nbytes(*tensors) -> int:
+    return sum(t.numel() * t.element_size() for t in tensors)
+
+
+class OpWorkload:
+    """One op's step on device buffers: ``step()`` runs it through the C-ABI,
+    ``inputs`` / ``outputs`` are the tensors e2e copies in / out, ``bytes`` the
+    compulsory HBM bytes of a step, ``launches`` our kernels per step."""
+
+    def __init__(self, op: str, device):
+        from muspace_b200.runtime.native import native_function
+
+        self.op = op
+        if op == "deformable_aggregation":
+            (mc, sp, st, loc, w), grad = cases.deformable_aggregation_inputs(device)
+            out = torch.empty(mc.shape[0], loc.shape[1], mc.shape[2], device=device)
+            gmc, gl, gw = torch.empty_like(mc), torch.empty_like(loc), torch.empty_like(w)
+            fwd = native_function("deformable_aggregation_forward_opt")
+            bwd = native_function("deformable_aggregation_backward_opt")
+
+            def step():
+                fwd(mc, sp, st, loc, w, out)
+                gmc.zero_()  # accumulated into, as the reference's autograd zero-fills it
+                bwd(mc, sp, st, loc, w, grad, gmc, gl, gw)
+
+            self.inputs, self.outputs = [mc, loc, w, grad], [out, gmc, gl, gw]
+            self.bytes = 2 * _nbytes(mc, loc, w) + _nbytes(out, grad, gmc, gl, gw)
+            self.launches = 2
+            self.workload = ("SparseDrive deformable aggregation fwd+bwd, reference production shapes: mc_ms_feat "
+                             "[8, 89760, 256] fp32, 6 cams x 4 scales, 900 anchors x 13 pts, 8 groups, 40% in image")
+            self.dtype = "f32"
+        elif op == "flash_sca":
+            t, kw = cases.flash_sca_inputs(device)
+            value, proj, shapes, starts, image, offsets, weights = t
+            gx, gy, gz = kw["grid_size"]
+            (sx, sy, sz), (x0, y0, z0) = kw["voxel_size"], kw["voxel_min"]
+            out = torch.empty(value.shape[0], gy, gx, value.shape[3], device=device)
+            grad = torch.randn(out.shape, generator=torch.Generator().manual_seed(3)).to(device)
+            roi = torch.tensor([x0, x0 + gx * sx, y0, y0 + gy * sy, z0, z0 + gz * sz], device=device)
+            gv, go, gwt = torch.empty_like(value), torch.empty_like(offsets), torch.empty_like(weights)
+            heads, points = offsets.shape[3], offsets.shape[5]
+            fwd = native_function("flash_bevpool_sca_forward")
+            bwd = native_function("flash_bevpool_sca_backward")
+
+            def step():
+                fwd(value, proj, shapes, starts, image, offsets, weights, out, heads, points, gx, gy, gz, sx, sy, sz,
+                    x0, y0, z0, value.shape[2], 1e-5)
+                for buf in (gv, go, gwt):  # accumulated into (the reference's autograd zero-fills them)
+                    buf.zero_()
+                bwd(grad, value, proj, shapes, starts, image, roi, offsets, weights, gv, go, gwt, heads, points, gx,
+                    gy, gz, value.shape[2], 1e-5)
+
+            self.inputs, self.outputs = [value, proj, offsets, weights, grad], [out, gv, go, gwt]
+            self.bytes = 2 * _nbytes(value, proj, offsets, weights) + _nbytes(out, grad, gv, go, gwt)
+            self.launches = 2
+            self.workload = ("FlashSCA fwd+bwd, BEVFormer-base: 200x200x4 BEV grid, 6 cams, 4 levels of a 480x800 "
+                             "image, 8 heads x 32 channels, 2 points per height, fp32")
+            self.dtype = "f32"
+        else:
+            inp, indexes, count, slots = cases.sca_scatter_inputs(device)
+            names = ("value", "spatial_shapes", "level_start_index", "sampling_locations", "attention_weights")
+            args = [inp[k] for k in names]
+            scatter = native_function("ms_deform_attn_scatter_div_forward")
+
+            def step():
+                slots.zero_()
+                for cam, index in enumerate(indexes):
+                    scatter(*args, index, count, slots, cam)
+
+            valid = sum(int(i.numel()) for i in indexes)
+            loc, w = inp["sampling_locations"], inp["attention_weights"]
+            per_row = (loc[0, 0].numel() + w[0, 0].numel()) * loc.element_size()  # one rebatched query, all heads
+            self.inputs, self.outputs = [inp["value"], loc, w, count], [slots]
+            self.bytes = (_nbytes(inp["value"], count) + valid * per_row + valid * 8
+                          + 2 * valid * slots.shape[2] * slots.element_size())
+            self.launches = len(indexes)
+            self.workload = ("BEVFormer-base SCA forward + rebatch scatter + count normalisation, 6 cameras x 10000 "
+                             "rebatched queries (6000-10000 valid), 40000 BEV queries, 8 heads x 32 channels, bf16")
+            self.dtype = "bf16"
+        self.step = step
+
+
+def _op_cpu_baseline(op: str, step_bytes: int):
+    """The op's CPU restatement (oracle/) on a bounded sample of the workload,
+    all host threads. The value is in the GPU line's units: the full step's
+    compulsory bytes over the sample's time scaled to the full step's work
+    (anchor rows, BEV cells or valid rebatched queries)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    if op == "deformable_aggregation":
+        from oracle.deformable_aggregation import deformable_aggregation_forward_backward
+
+        (mc, sp, st, loc, w), grad = cases.deformable_aggregation_inputs("cpu", batch=1, anchors=64)
+        run = lambda: deformable_aggregation_forward_backward(mc, sp, st, loc, w, grad)  # noqa: E731
+        scale, sample = 8 * 900 / 64, "64 anchor rows of the 8 x 900 (batch 1)"
+    elif op == "flash_sca":
+        from oracle.flash_sca import flash_sca_forward_backward
+
+        t, kw = cases.flash_sca_inputs("cpu", grid=(20, 20, 4))
+        grad = torch.randn(1, 20, 20, t[0].shape[3])
+        run = lambda: flash_sca_forward_backward(*t, kw["grid_size"], kw["voxel_size"], kw["voxel_min"], grad)  # noqa: E731
+        scale, sample = 200 * 200 / (20 * 20), "a 20x20x4 BEV patch of the 200x200x4 grid, all cameras"
+    else:
+        from oracle import oracle_scatter_div
+
+        inp, indexes, count, slots = cases.sca_scatter_inputs("cpu", dtype=torch.float32, cams=1, max_len=1000,
+                                                              num_query=4000, lens=(1000,))
+        names = ("value", "spatial_shapes", "level_start_index", "sampling_locations", "attention_weights")
+        arrays = [inp[k].numpy() for k in names]
+        run = lambda: oracle_scatter_div(*arrays, indexes[0].numpy(), count.numpy(), slots.numpy(), 0)  # noqa: E731
+        scale, sample = 50000 / 1000, "1000 of the 50000 valid rebatched queries, one camera (C oracle, fp32)"
+    run()
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(step_bytes / (t * scale) / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{sample}; median of 3 after 1 warm-up, {t * 1e3:.1f} ms per sample, x{scale:g} to a step",
+            "ms_per_step": round(t * scale * 1e3, 1)}
+
+
+def run_op(args, rank, world, device):
+    """--op: K timed steps of one op on device-resident inputs (each rank an
+    independent replica, weak scaling), then the e2e leg with pinned host
+    buffers and the CPU baseline on rank 0."""
+    import torch.distributed as dist
+
+    w = OpWorkload(args.op, device)
+    for _ in range(args.warmup):
+        w.step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device.index) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            w.step()
+        end.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    e2e = None
+    if not args.no_e2e:
+        host_in = [x.cpu().pin_memory() for x in w.inputs]
+        host_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in w.outputs]
+
+        def one():
+            for dst, src in zip(w.inputs, host_in):
+                dst.copy_(src, non_blocking=True)
+            w.step()
+            for dst, src in zip(host_out, w.outputs):
+                dst.copy_(src, non_blocking=True)
+
+        one()
+        torch.cuda.synchronize()
+        steps = max(3, min(args.steps, 10))
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(steps):
+            one()
+        e2.record()
+        torch.cuda.synchronize()
+        t2 = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t2.item()) / steps
+        e2e = {"value": round(w.bytes * world / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": _nbytes(*host_in), "d2h_bytes_per_step": _nbytes(*host_out),
+               "ms_per_step": round(e2e_ms, 3), "steps": steps}
+    if rank != 0:
+        return None
+    peak, peak_src = _peaks()
+    achieved = w.bytes / (ms / 1e3) / 1e9
+    line = {
+        "metric": f"{args.op} step us & effective HBM GB/s (compulsory bytes / device time)",
+        "value": round(achieved * world, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "us_per_call": round(ms * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": w.dtype,
+        "data": "synthetic",
+        "config": {"workload": w.workload, "parallelism": f"{world} independent replicas",
+                   "compulsory_bytes_per_step": w.bytes, "l2": "inputs > 126 MB L2; no flush"},
+        "roofline": {"bound": "hbm", "kernel": f"{args.op} step", "achieved": round(achieved, 1), "peak": peak,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None},
+        "gpu_launches": w.launches * args.steps * world,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = _op_cpu_baseline(args.op, w.bytes)
+    return line
+
+
 def main():
     args = parse_args()
     cfg = cases.CONFIGS[args.config]
@@ -506,7 +718,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
     try:
-        line = run_b200(args, cfg, dtype, rank, world, device)
+        line = run_op(args, rank, world, device) if args.op != "msda" else run_b200(args, cfg, dtype, rank, world, device)
     finally:
         if world > 1:
             import torch.distributed as dist

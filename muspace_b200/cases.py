@@ -17,6 +17,7 @@ Layouts follow the operator: value ``(B, Lin, Hh, D)``, sampling_locations
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field, replace
 
 import torch
@@ -221,3 +222,89 @@ def compulsory_bytes(cfg: MSDAConfig, dtype: torch.dtype, scope: str = "fwd+bwd"
     if scope == "fwd":
         return {"fwd": fwd, "bwd": 0, "total": fwd}
     return {"fwd": fwd, "bwd": bwd, "total": fwd + bwd}
+
+
+# ---------------------------------------------------------------------------
+# workloads of the ops next to MSDA (deformable aggregation, FlashSCA, the
+# fused SCA scatter): seeded synthetic tensors with the reference's shapes
+# ---------------------------------------------------------------------------
+SPARSEDRIVE_SHAPES = ((64, 176), (32, 88), (16, 44), (8, 22))
+
+
+def deformable_aggregation_inputs(device, *, batch=8, anchors=900, pts=13, cams=6, channels=256, groups=8,
+                                  active=0.40, seed=0):
+    """The reference test's SparseDrive production shapes
+    (``tests/ops/test_deformable_aggregation.py:29-79`` in the muSPACE tree):
+    mc_ms_feat [B, 6 * 14960, 256], 6 cameras x 4 scales
+    [(64,176),(32,88),(16,44),(8,22)], 900 anchors x 13 points, 8 groups; a
+    fraction ``active`` of the (pt, cam) pairs lies inside the image, the rest
+    at N(0, 10) (outside); weights U(0, 0.004). Returns the five inputs and a
+    N(0, 1) grad_output."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    sizes = [h * w for h, w in SPARSEDRIVE_SHAPES]
+    spatial = torch.tensor([list(map(list, SPARSEDRIVE_SHAPES))] * cams, dtype=torch.int32)
+    start = torch.tensor([[sum(sizes) * c + sum(sizes[:s]) for s in range(len(sizes))] for c in range(cams)],
+                         dtype=torch.int32)
+    mc = torch.randn(batch, sum(sizes) * cams, channels, generator=g)
+    pshape = (batch, anchors, pts, cams)
+    inside_mask = torch.rand(*pshape, generator=g) < active
+    outside = torch.randn(*pshape, 2, generator=g) * 10.0
+    inside = torch.rand(*pshape, 2, generator=g) * 0.98 + 0.01
+    loc = torch.where(inside_mask.unsqueeze(-1), inside, outside)
+    weights = torch.rand(*pshape, len(sizes), groups, generator=g) * 0.004
+    grad = torch.randn(batch, anchors, channels, generator=g)
+    return [x.to(device) for x in (mc, spatial, start, loc, weights)], grad.to(device)
+
+
+def pinhole_cameras(batch, cams, image_hw, gen, height=1.5):
+    """Cameras at (0, 0, height) looking outwards at evenly spread yaws (with a
+    little seeded jitter): 3x4 projection matrices [B, cams, 3, 4]."""
+    img_h, img_w = image_hw
+    mats = torch.zeros(batch, cams, 3, 4)
+    for b in range(batch):
+        for c in range(cams):
+            yaw = 2 * math.pi * c / cams + float(torch.randn((), generator=gen)) * 0.05
+            rot = torch.tensor([[math.sin(yaw), -math.cos(yaw), 0.0], [0.0, 0.0, -1.0],
+                                [math.cos(yaw), math.sin(yaw), 0.0]])
+            k = torch.tensor([[img_w * 0.5, 0.0, img_w * 0.5], [0.0, img_h * 0.5, img_h * 0.5], [0.0, 0.0, 1.0]])
+            mats[b, c, :, :3] = k @ rot
+            mats[b, c, :, 3] = k @ (-(rot @ torch.tensor([0.0, 0.0, height])))
+    return mats
+
+
+def flash_sca_inputs(device, *, batch=1, cams=6, grid=(200, 200, 4), channels=256, heads=8, points=2, seed=5):
+    """BEVFormer-base spatial cross-attention without rebatching: 6 cameras
+    around the ego car, 4 levels of a 480x800 image, 8 heads x 32 channels,
+    a 200x200 BEV grid over [-51.2, 51.2]^2 with 4 heights in [-5, 3], 2
+    points per height. Returns the seven tensors and the grid keywords."""
+    g = torch.Generator().manual_seed(seed)
+    image_hw = (480, 800)
+    shapes = [(60, 100), (30, 50), (15, 25), (8, 13)]
+    sizes = [h * w for h, w in shapes]
+    value = torch.randn(batch, cams, sum(sizes), channels, generator=g)
+    proj = pinhole_cameras(batch, cams, image_hw, g)
+    gx, gy, gz = grid
+    offsets = torch.randn(batch, gy, gx, heads, len(shapes), points, gz, 2, generator=g) * 2.0
+    weights = torch.rand(batch, gy, gx, heads, len(shapes), points, gz, generator=g) / (len(shapes) * points * gz)
+    tensors = [value, proj, torch.tensor(shapes, dtype=torch.int32),
+               torch.tensor([sum(sizes[:i]) for i in range(len(shapes))], dtype=torch.int32),
+               torch.tensor(image_hw, dtype=torch.int32), offsets, weights]
+    kw = dict(grid_size=grid, voxel_size=(102.4 / gx, 102.4 / gy, 8.0 / gz), voxel_min=(-51.2, -51.2, -5.0))
+    return [x.to(device) for x in tensors], kw
+
+
+def sca_scatter_inputs(device, *, dtype=torch.bfloat16, batch=1, cams=6, max_len=10000, num_query=40000,
+                       lens=(10000, 9000, 8000, 10000, 7000, 6000), seed=0):
+    """BEVFormer-base rebatched SCA: the c2 MSDA shapes for the B * 6 camera
+    images (max_len rebatched queries each), each camera seeing ``lens[cam]``
+    distinct BEV queries of 40000, count = cameras per BEV query (min 1)."""
+    cfg = CONFIGS["c2"].with_(batch=batch * cams, queries=max_len)
+    inp = make_inputs(cfg, dtype=dtype, seed=2333 + seed, device=device, with_grad=False)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    indexes = [torch.randperm(num_query, generator=g)[:n].sort().values.to(device) for n in lens[:cams]]
+    count = torch.zeros(batch, num_query, device=device)
+    for idx in indexes:
+        count[:, idx] += 1
+    count = count.clamp_(min=1).to(dtype)
+    slots = torch.zeros(batch, num_query, cfg.heads * cfg.channels, dtype=dtype, device=device)
+    return inp, indexes, count, slots

@@ -20,6 +20,7 @@ import pytest
 import torch
 
 from conftest import ROOT
+from muspace_b200 import cases
 from muspace_b200.ops import deformable_aggregation, feature_maps_format
 from muspace_b200.runtime import native
 from oracle.deformable_aggregation import deformable_aggregation_forward_backward
@@ -210,23 +211,8 @@ def test_zero_anchors_return_empty_output_and_zero_gradients(cuda_device):
 
 
 def _production_inputs(device, batch, anchors, seed=0):
-    """The reference test's production shapes (tests/ops/test_deformable_aggregation.py:29-79):
-    6 cameras x 4 scales [(64,176),(32,88),(16,44),(8,22)], 13 points, 8 groups, C = 256,
-    40 % of (pt, cam) pairs inside the image; fewer batch entries / anchors on request."""
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    shapes = [[64, 176], [32, 88], [16, 44], [8, 22]]
-    sizes = [h * w for h, w in shapes]
-    spatial = torch.tensor([shapes] * 6, dtype=torch.int32)
-    start = torch.tensor([[sum(sizes) * c + sum(sizes[:s]) for s in range(4)] for c in range(6)], dtype=torch.int32)
-    mc = torch.randn(batch, 89760, 256, generator=g)
-    pshape = (batch, anchors, 13, 6)
-    active = torch.rand(*pshape, generator=g) < 0.40
-    outside = torch.randn(*pshape, 2, generator=g) * 10.0
-    inside = torch.rand(*pshape, 2, generator=g) * 0.98 + 0.01
-    loc = torch.where(active.unsqueeze(-1), inside, outside)
-    weights = torch.rand(*pshape, 4, 8, generator=g) * 0.004
-    grad = torch.randn(batch, anchors, 256, generator=g)
-    return [x.to(device) for x in (mc, spatial, start, loc, weights)], grad.to(device)
+    """The reference test's production shapes (cases.deformable_aggregation_inputs)."""
+    return cases.deformable_aggregation_inputs(device, batch=batch, anchors=anchors, seed=seed)
 
 
 @pytest.mark.gpu

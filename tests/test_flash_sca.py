@@ -13,13 +13,13 @@ from __future__ import annotations
 
 import hashlib
 import json
-import math
 
 import numpy as np
 import pytest
 import torch
 
 from conftest import ROOT
+from muspace_b200 import cases
 from muspace_b200.ops import flash_bevpool_sca
 from muspace_b200.runtime import native
 from oracle.flash_sca import flash_sca_forward_backward
@@ -124,40 +124,13 @@ def test_roi_range_equals_voxel_size_and_min(cuda_device):
     torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
 
 
-def _cameras(batch, cams, image_hw, gen, height=1.5):
-    img_h, img_w = image_hw
-    mats = torch.zeros(batch, cams, 3, 4)
-    for b in range(batch):
-        for c in range(cams):
-            yaw = 2 * math.pi * c / cams + float(torch.randn((), generator=gen)) * 0.05
-            rot = torch.tensor([[math.sin(yaw), -math.cos(yaw), 0.0], [0.0, 0.0, -1.0],
-                                [math.cos(yaw), math.sin(yaw), 0.0]])
-            k = torch.tensor([[img_w * 0.5, 0.0, img_w * 0.5], [0.0, img_h * 0.5, img_h * 0.5], [0.0, 0.0, 1.0]])
-            mats[b, c, :, :3] = k @ rot
-            mats[b, c, :, 3] = k @ (-(rot @ torch.tensor([0.0, 0.0, height])))
-    return mats
-
-
-def bevformer_inputs(device, *, batch=1, cams=6, grid=(50, 50, 4), channels=256, heads=8, points=4, seed=5):
-    g = torch.Generator().manual_seed(seed)
-    image_hw = (480, 800)
-    shapes = [(60, 100), (30, 50), (15, 25), (8, 13)]
-    sizes = [h * w for h, w in shapes]
-    value = torch.randn(batch, cams, sum(sizes), channels, generator=g)
-    proj = _cameras(batch, cams, image_hw, g)
-    gx, gy, gz = grid
-    offsets = torch.randn(batch, gy, gx, heads, len(shapes), points, gz, 2, generator=g) * 2.0
-    weights = torch.rand(batch, gy, gx, heads, len(shapes), points, gz, generator=g) / (len(shapes) * points * gz)
-    t = [value, proj, torch.tensor(shapes, dtype=torch.int32),
-         torch.tensor([sum(sizes[:i]) for i in range(len(shapes))], dtype=torch.int32),
-         torch.tensor(image_hw, dtype=torch.int32), offsets, weights]
-    kw = dict(grid_size=grid, voxel_size=(102.4 / gx, 102.4 / gy, 8.0 / gz), voxel_min=(-51.2, -51.2, -5.0))
-    return [x.to(device) for x in t], kw
+def bevformer_inputs(device, **kw):
+    return cases.flash_sca_inputs(device, **kw)
 
 
 @pytest.mark.gpu
 def test_bevformer_like_case_matches_the_oracle(cuda_device):
-    t, kw = bevformer_inputs(cuda_device, grid=(24, 24, 4))
+    t, kw = bevformer_inputs(cuda_device, grid=(24, 24, 4), points=4)
     leaves = list(t)
     for i in (0, 5, 6):
         leaves[i] = t[i].clone().requires_grad_(True)
