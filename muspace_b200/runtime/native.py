@@ -69,14 +69,13 @@ _DTYPE_CODES = {
 
 
 class _View:
-    """A DLTensor describing ``tensor`` plus the arrays it points into."""
+    """A DLTensor describing a tensor, plus the shape and stride arrays it points into."""
 
-    __slots__ = ("tensor", "shape", "strides", "dl")
+    __slots__ = ("shape", "strides", "dl")
 
     def __init__(self, tensor: torch.Tensor):
         if tensor.dtype not in _DTYPE_CODES:
             raise TypeError(f"unsupported tensor dtype {tensor.dtype}")
-        self.tensor = tensor
         ndim = tensor.dim()
         self.shape = (ctypes.c_int64 * max(ndim, 1))(*tensor.shape)
         self.strides = (ctypes.c_int64 * max(ndim, 1))(*tensor.stride())
@@ -94,6 +93,24 @@ class _View:
             ctypes.cast(self.strides, ctypes.POINTER(ctypes.c_int64)),
             0,
         )
+
+
+# Descriptors by (data pointer, dtype, device, shape, strides): every field of a
+# DLTensor, so a hit describes the argument exactly even when the memory it was
+# first built for has since been freed and handed to another tensor. Building a
+# descriptor costs ~9 us of Python; a per-camera launch loop reuses the same few.
+_VIEW_CACHE: dict[tuple, _View] = {}
+_VIEW_CACHE_LIMIT = 1024
+
+
+def _view_of(tensor: torch.Tensor) -> _View:
+    key = (tensor.data_ptr(), tensor.dtype, tensor.device, tensor.shape, tensor.stride())
+    view = _VIEW_CACHE.get(key)
+    if view is None:
+        if len(_VIEW_CACHE) >= _VIEW_CACHE_LIMIT:
+            _VIEW_CACHE.clear()
+        view = _VIEW_CACHE[key] = _View(tensor)
+    return view
 
 
 def _stream_of(tensors) -> int:
@@ -162,7 +179,7 @@ class NativeModule:
                 if kind == "t":
                     if not isinstance(arg, torch.Tensor):
                         raise TypeError(f"{name}: expected a tensor, got {type(arg).__name__}")
-                    view = _View(arg)
+                    view = _view_of(arg)
                     views.append(view)
                     c_args.append(ctypes.byref(view.dl))
                 elif kind == "f":

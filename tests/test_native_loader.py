@@ -51,3 +51,19 @@ def test_op_reports_unavailable_library(monkeypatch):
             torch.zeros(1, 1, 1, 1, 1, 2),
             torch.ones(1, 1, 1, 1, 1),
         )
+
+
+def test_tensor_descriptors_are_reused_only_for_identical_views():
+    import torch
+
+    t = torch.zeros(3, 4, 5)
+    a = native._view_of(t)
+    assert native._view_of(t) is a
+    assert native._view_of(t.view(3, 4, 5)) is a  # another tensor object, same description
+    for other in (t.transpose(0, 1), t[1:], t.view(12, 5), t.to(torch.float64), torch.zeros(3, 4, 5)):
+        v = native._view_of(other)
+        assert v is not a
+        assert v.dl.data == (other.data_ptr() or None)
+        assert v.dl.ndim == other.dim()
+        assert [v.shape[i] for i in range(other.dim())] == list(other.shape)
+        assert [v.strides[i] for i in range(other.dim())] == list(other.stride())
