@@ -18,7 +18,10 @@
 // geometry of 32 (pair, scale) samples at a time in shared memory (one sample
 // per lane: four corner rows, four bilinear weights, the group weights), and
 // every lane walks the staged samples gathering its slices. The forward keeps
-// the row in registers and stores it once: no atomics. The backward forms per
+// the row in registers and stores it once: no atomics. The backward, whose
+// outputs are all per (pt, cam), gives a warp one camera's pairs of the row,
+// (b, cam, anchor) items with anchors fastest, so that the resident warps share
+// one camera's maps and their gradients in L2. It forms per
 // corner the dot of grad_output with the gathered slice (4 per lane and
 // sample), from which a shuffle reduction over the lanes of a group gives the
 // weight gradient and a reduction over the warp, once per pair, the location
@@ -26,6 +29,18 @@
 // slices. The scalar kernels below cover every other shape and serve the
 // "base" entry points.
 #include "deform_agg.h"
+
+// 1: the forward also runs camera-major, each (b, cam, anchor) warp adding its
+// camera's partial row into the zero-filled output with vector REDs (the
+// summation order over cameras then varies between runs, as in the
+// reference's atomicAdd kernels); 0: one warp per (b, anchor) row, stored once.
+#ifndef DA_FWD_CAM_MAJOR
+#define DA_FWD_CAM_MAJOR 1
+#endif
+// 1: the backward runs camera-major (below); 0: one warp per (b, anchor) row.
+#ifndef DA_BWD_CAM_MAJOR
+#define DA_BWD_CAM_MAJOR 1
+#endif
 
 namespace da {
 namespace {
@@ -100,17 +115,19 @@ struct Stage {
   float wg[32][kMaxGroups];
 };
 
-// Compacts the in-image pairs of pairs [p0, p0 + 32) of a row into st.pair /
-// st.loc; returns how many there are. Lanes of out-of-image pairs call
-// on_outside(p) (the backward zeroes their gradients there).
+// Compacts the in-image pairs among p = first + i * step, i in [i0, min(i0 + 32,
+// count)), of a row into st.pair / st.loc; returns how many there are. Lanes
+// of out-of-image pairs call on_outside(p) (the backward zeroes their
+// gradients there).
 template <typename F>
-__device__ __forceinline__ int compact_pairs(const float* loc_row, int p0, int pairs, int d_scales, Stage& st,
-                                             F&& on_outside) {
+__device__ __forceinline__ int compact_pairs(const float* loc_row, int first, int step, int i0, int count,
+                                             int d_scales, Stage& st, F&& on_outside) {
   const int lane = threadIdx.x % 32;
-  const int p = p0 + lane;
+  const int i = i0 + lane;
+  const int p = first + i * step;
   float2 l = make_float2(0.0f, 0.0f);
   bool act = false;
-  if (p < pairs) {
+  if (i < count) {
     l = __ldg(reinterpret_cast<const float2*>(loc_row) + p);
     act = inside(l) && d_scales > 0;  // without scales an in-image pair contributes nothing either
     if (!act) on_outside(p);
@@ -156,11 +173,23 @@ __global__ void __launch_bounds__(kThreads) forward_vec(Dims d, const float* __r
   __shared__ Stage stage[kWarps];
   stage_maps(maps, shape, start, d);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  Stage& st = stage[warp];
+  const int pairs = d.pts * d.cams;
+#if DA_FWD_CAM_MAJOR
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  if (item >= static_cast<int64_t>(d.batch) * d.cams * d.anchors) return;  // whole warp
+  const int64_t bc = item / d.anchors;
+  const int cam = static_cast<int>(bc % d.cams);
+  const int64_t b = bc / d.cams;
+  const int64_t row = b * d.anchors + (item - bc * d.anchors);
+  const int first = cam, step = d.cams, count = d.pts;
+  bool any = false;
+#else
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
   if (row >= static_cast<int64_t>(d.batch) * d.anchors) return;  // whole warp
-  Stage& st = stage[warp];
   const int64_t b = row / d.anchors;
-  const int pairs = d.pts * d.cams;
+  const int first = 0, step = 1, count = pairs;
+#endif
   const int slices = d.channels / 4;
   const int per_group = d.channels / d.groups;
   const float* fb = feat + b * d.num_feat * static_cast<int64_t>(d.channels);
@@ -171,8 +200,11 @@ __global__ void __launch_bounds__(kThreads) forward_vec(Dims d, const float* __r
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) acc[r] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 
-  for (int p0 = 0; p0 < pairs; p0 += 32) {
-    const int n = compact_pairs(loc_row, p0, pairs, d.scales, st, [](int) {});
+  for (int p0 = 0; p0 < count; p0 += 32) {
+    const int n = compact_pairs(loc_row, first, step, p0, count, d.scales, st, [](int) {});
+#if DA_FWD_CAM_MAJOR
+    any |= n > 0;
+#endif
     const int total = n * d.scales;
     for (int q0 = 0; q0 < total; q0 += 32) {
       stage_sample(d, maps, w_row, q0, total, st);
@@ -206,11 +238,20 @@ __global__ void __launch_bounds__(kThreads) forward_vec(Dims d, const float* __r
       __syncwarp();  // the next staging overwrites the slots read above
     }
   }
+#if DA_FWD_CAM_MAJOR
+  if (!any) return;  // warp-uniform: no in-image pair of this camera
+#pragma unroll
+  for (int r = 0; r < kRounds; ++r) {
+    const int slice = lane + 32 * r;
+    if (slice < slices) red4(out + row * d.channels + slice * 4, acc[r].x, acc[r].y, acc[r].z, acc[r].w);
+  }
+#else
 #pragma unroll
   for (int r = 0; r < kRounds; ++r) {
     const int slice = lane + 32 * r;
     if (slice < slices) *reinterpret_cast<float4*>(out + row * d.channels + slice * 4) = acc[r];
   }
+#endif
 }
 
 // Sum over aligned groups of `width` lanes (a power of two).
@@ -231,11 +272,26 @@ __global__ void __launch_bounds__(kThreads) backward_vec(Dims d, const float* __
   __shared__ Stage stage[kWarps];
   stage_maps(maps, shape, start, d);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // item = (b, cam, anchor), anchors fastest: the warps resident at one time
+  // work on one or two cameras' maps of one batch element, whose features and
+  // feature gradients (2 x 15 MB at the production shapes) stay in L2, where a
+  // warp per (b, anchor) spread them over all six cameras of several elements.
+  Stage& st = stage[warp];
+  const int pairs = d.pts * d.cams;
+#if DA_BWD_CAM_MAJOR
+  const int64_t item = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  if (item >= static_cast<int64_t>(d.batch) * d.cams * d.anchors) return;  // whole warp
+  const int64_t bc = item / d.anchors;
+  const int cam = static_cast<int>(bc % d.cams);
+  const int64_t b = bc / d.cams;
+  const int64_t row = b * d.anchors + (item - bc * d.anchors);
+  const int first = cam, step = d.cams, count = d.pts;  // this camera's pairs pt * cams + cam
+#else
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
   if (row >= static_cast<int64_t>(d.batch) * d.anchors) return;  // whole warp
-  Stage& st = stage[warp];
   const int64_t b = row / d.anchors;
-  const int pairs = d.pts * d.cams;
+  const int first = 0, step = 1, count = pairs;
+#endif
   const int slices = d.channels / 4;
   const int per_group = d.channels / d.groups;
   const int group_lanes = per_group / 4;  // lanes holding one group's channels (a power of two)
@@ -255,8 +311,8 @@ __global__ void __launch_bounds__(kThreads) backward_vec(Dims d, const float* __
   }
 
   float lx = 0.0f, ly = 0.0f;  // this lane's share of the current pair's location gradient
-  for (int p0 = 0; p0 < pairs; p0 += 32) {
-    const int n = compact_pairs(loc_row, p0, pairs, d.scales, st, [&](int p) {
+  for (int p0 = 0; p0 < count; p0 += 32) {
+    const int n = compact_pairs(loc_row, first, step, p0, count, d.scales, st, [&](int p) {
       *reinterpret_cast<float2*>(gl_row + 2 * p) = make_float2(0.0f, 0.0f);
       for (int64_t i = 0; i < w_per_pair; ++i) gw_row[p * w_per_pair + i] = 0.0f;
     });
@@ -435,7 +491,16 @@ cudaError_t forward(const Dims& d, const Args& a, bool optimized, cudaStream_t s
   const int rounds = optimized ? vec_rounds(d, a, false) : 0;
   const size_t smem = map_smem(d);
   if (rounds) {
-    const int grid = static_cast<int>((rows + kWarps - 1) / kWarps);
+#if DA_FWD_CAM_MAJOR
+    const cudaError_t zero =
+        cudaMemsetAsync(a.out, 0, static_cast<size_t>(rows) * d.channels * sizeof(float), stream);
+    if (zero != cudaSuccess) return zero;
+    const int64_t items = rows * d.cams;
+    if (items == 0) return cudaSuccess;
+#else
+    const int64_t items = rows;
+#endif
+    const int grid = static_cast<int>((items + kWarps - 1) / kWarps);
     switch (rounds) {
       case 1: forward_vec<1><<<grid, kThreads, smem, stream>>>(d, a.feat, a.shape, a.start, a.loc, a.weights, a.out); break;
       case 2: forward_vec<2><<<grid, kThreads, smem, stream>>>(d, a.feat, a.shape, a.start, a.loc, a.weights, a.out); break;
@@ -454,7 +519,13 @@ cudaError_t backward(const Dims& d, const Args& a, bool optimized, cudaStream_t 
   const int rounds = optimized ? vec_rounds(d, a, true) : 0;
   const size_t smem = map_smem(d);
   if (rounds) {
-    const int grid = static_cast<int>((rows + kWarps - 1) / kWarps);
+#if DA_BWD_CAM_MAJOR
+    const int64_t items = rows * d.cams;
+    if (items == 0) return cudaSuccess;  // no cameras: nothing to write either
+#else
+    const int64_t items = rows;
+#endif
+    const int grid = static_cast<int>((items + kWarps - 1) / kWarps);
     switch (rounds) {
       case 1: backward_vec<1><<<grid, kThreads, smem, stream>>>(d, a.feat, a.shape, a.start, a.loc, a.weights, a.grad_out, a.grad_feat, a.grad_loc, a.grad_weights); break;
       case 2: backward_vec<2><<<grid, kThreads, smem, stream>>>(d, a.feat, a.shape, a.start, a.loc, a.weights, a.grad_out, a.grad_feat, a.grad_loc, a.grad_weights); break;
