@@ -497,9 +497,12 @@ def _nbytes(*tensors) -> int:
 
 
 class OpWorkload:
-    """One op's step on device buffers: ``step()`` runs it through the C-ABI,
-    ``inputs`` / ``outputs`` are the tensors e2e copies in / out, ``bytes`` the
-    compulsory HBM bytes of a step, ``launches`` our kernels per step."""
+    """One op's step on device buffers, as a list of phases (name, call,
+    algorithmic bytes, our kernel launches; the fills that the reference's
+    autograd performs count no bytes and no launches). ``inputs`` / ``outputs``
+    are the tensors e2e copies in / out, ``bytes`` the compulsory HBM bytes of
+    a step, ``dominant`` the phase the roofline is quoted on with its
+    ``profiles/dram_traffic.json`` key and units (launch_units)."""
 
     def __init__(self, op: str, device):
         from muspace_b200.runtime.native import native_function
@@ -511,15 +514,15 @@ class OpWorkload:
             gmc, gl, gw = torch.empty_like(mc), torch.empty_like(loc), torch.empty_like(w)
             fwd = native_function("deformable_aggregation_forward_opt")
             bwd = native_function("deformable_aggregation_backward_opt")
-
-            def step():
-                fwd(mc, sp, st, loc, w, out)
-                gmc.zero_()  # accumulated into, as the reference's autograd zero-fills it
-                bwd(mc, sp, st, loc, w, grad, gmc, gl, gw)
-
+            self.phases = [
+                ("forward", lambda: fwd(mc, sp, st, loc, w, out), _nbytes(mc, loc, w, out), 1),
+                # accumulated into, as the reference's autograd zero-fills it
+                ("grad_fill", gmc.zero_, 0, 0),
+                ("backward", lambda: bwd(mc, sp, st, loc, w, grad, gmc, gl, gw),
+                 _nbytes(mc, loc, w, grad, gmc, gl, gw), 1),
+            ]
+            self.dominant = ("backward", "deformable_aggregation_backward", 1)
             self.inputs, self.outputs = [mc, loc, w, grad], [out, gmc, gl, gw]
-            self.bytes = 2 * _nbytes(mc, loc, w) + _nbytes(out, grad, gmc, gl, gw)
-            self.launches = 2
             self.workload = ("SparseDrive deformable aggregation fwd+bwd, reference production shapes: mc_ms_feat "
                              "[8, 89760, 256] fp32, 6 cams x 4 scales, 900 anchors x 13 pts, 8 groups, 40% in image")
             self.dtype = "f32"
@@ -536,17 +539,21 @@ class OpWorkload:
             fwd = native_function("flash_bevpool_sca_forward")
             bwd = native_function("flash_bevpool_sca_backward")
 
-            def step():
-                fwd(value, proj, shapes, starts, image, offsets, weights, out, heads, points, gx, gy, gz, sx, sy, sz,
-                    x0, y0, z0, value.shape[2], 1e-5)
-                for buf in (gv, go, gwt):  # accumulated into (the reference's autograd zero-fills them)
+            def fill():  # accumulated into (the reference's autograd zero-fills them)
+                for buf in (gv, go, gwt):
                     buf.zero_()
-                bwd(grad, value, proj, shapes, starts, image, roi, offsets, weights, gv, go, gwt, heads, points, gx,
-                    gy, gz, value.shape[2], 1e-5)
 
+            self.phases = [
+                ("forward", lambda: fwd(value, proj, shapes, starts, image, offsets, weights, out, heads, points, gx,
+                                        gy, gz, sx, sy, sz, x0, y0, z0, value.shape[2], 1e-5),
+                 _nbytes(value, proj, offsets, weights, out), 1),
+                ("grad_fill", fill, 0, 0),
+                ("backward", lambda: bwd(grad, value, proj, shapes, starts, image, roi, offsets, weights, gv, go, gwt,
+                                         heads, points, gx, gy, gz, value.shape[2], 1e-5),
+                 _nbytes(value, proj, offsets, weights, grad, gv, go, gwt), 1),
+            ]
+            self.dominant = ("backward", "flash_sca_backward", 1)
             self.inputs, self.outputs = [value, proj, offsets, weights, grad], [out, gv, go, gwt]
-            self.bytes = 2 * _nbytes(value, proj, offsets, weights) + _nbytes(out, grad, gv, go, gwt)
-            self.launches = 2
             self.workload = ("FlashSCA fwd+bwd, BEVFormer-base: 200x200x4 BEV grid, 6 cams, 4 levels of a 480x800 "
                              "image, 8 heads x 32 channels, 2 points per height, fp32")
             self.dtype = "f32"
@@ -556,22 +563,29 @@ class OpWorkload:
             args = [inp[k] for k in names]
             scatter = native_function("ms_deform_attn_scatter_div_forward")
 
-            def step():
-                slots.zero_()
+            def cameras():
                 for cam, index in enumerate(indexes):
                     scatter(*args, index, count, slots, cam)
 
             valid = sum(int(i.numel()) for i in indexes)
             loc, w = inp["sampling_locations"], inp["attention_weights"]
             per_row = (loc[0, 0].numel() + w[0, 0].numel()) * loc.element_size()  # one rebatched query, all heads
+            scatter_bytes = (_nbytes(inp["value"], count) + valid * per_row + valid * 8
+                             + 2 * valid * slots.shape[2] * slots.element_size())
+            self.phases = [("slots_fill", slots.zero_, 0, 0),
+                           ("scatter", cameras, scatter_bytes, len(indexes))]
+            # traffic is recorded per valid rebatched query of a camera launch
+            self.dominant = ("scatter", "sca_scatter", valid)
             self.inputs, self.outputs = [inp["value"], loc, w, count], [slots]
-            self.bytes = (_nbytes(inp["value"], count) + valid * per_row + valid * 8
-                          + 2 * valid * slots.shape[2] * slots.element_size())
-            self.launches = len(indexes)
             self.workload = ("BEVFormer-base SCA forward + rebatch scatter + count normalisation, 6 cameras x 10000 "
                              "rebatched queries (6000-10000 valid), 40000 BEV queries, 8 heads x 32 channels, bf16")
             self.dtype = "bf16"
-        self.step = step
+        self.bytes = sum(p[2] for p in self.phases)
+        self.launches = sum(p[3] for p in self.phases)
+
+    def step(self):
+        for _, call, _, _ in self.phases:
+            call()
 
 
 def _op_cpu_baseline(op: str, step_bytes: int):
@@ -617,8 +631,9 @@ def _op_cpu_baseline(op: str, step_bytes: int):
 
 def run_op(args, rank, world, device):
     """--op: K timed steps of one op on device-resident inputs (each rank an
-    independent replica, weak scaling), then the e2e leg with pinned host
-    buffers and the CPU baseline on rank 0."""
+    independent replica, weak scaling), then K steps with CUDA events around
+    every phase (kernels_ms and the dominant kernel's roofline), the e2e leg
+    with pinned host buffers and the CPU baseline on rank 0."""
     import torch.distributed as dist
 
     w = OpWorkload(args.op, device)
@@ -638,6 +653,22 @@ def run_op(args, rank, world, device):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item()) / args.steps
+
+    # per-phase device time: events on the launching (current) stream around every phase
+    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in w.phases]
+              for _ in range(args.steps)]
+    for step_events in events:
+        for (a, b), (_, call, _, _) in zip(step_events, w.phases):
+            a.record()
+            call()
+            b.record()
+    torch.cuda.synchronize()
+    phase_ms = torch.tensor([sum(step_events[i][0].elapsed_time(step_events[i][1]) for step_events in events)
+                             / args.steps for i in range(len(w.phases))], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(phase_ms, op=dist.ReduceOp.MAX)
+    kernels_ms = {p[0]: round(float(v), 4) for p, v in zip(w.phases, phase_ms.tolist())}
+
     e2e = None
     if not args.no_e2e:
         host_in = [x.cpu().pin_memory() for x in w.inputs]
@@ -670,6 +701,11 @@ def run_op(args, rank, world, device):
         return None
     peak, peak_src = _peaks()
     achieved = w.bytes / (ms / 1e3) / 1e9
+    dom_name, dom_key, dom_units = w.dominant
+    dom = next(p for p in w.phases if p[0] == dom_name)
+    dom_ms = kernels_ms[dom_name]
+    dom_achieved = dom[2] / (dom_ms / 1e3) / 1e9
+    traffic, traffic_src = _traffic(dom_key, args.op, dom_units)
     line = {
         "metric": f"{args.op} step us & effective HBM GB/s (compulsory bytes / device time)",
         "value": round(achieved * world, 2),
@@ -679,6 +715,7 @@ def run_op(args, rank, world, device):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "us_per_call": round(ms * 1e3, 1),
+        "kernels_ms": kernels_ms,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -686,12 +723,16 @@ def run_op(args, rank, world, device):
         "data": "synthetic",
         "config": {"workload": w.workload, "parallelism": f"{world} independent replicas",
                    "compulsory_bytes_per_step": w.bytes, "l2": "inputs > 126 MB L2; no flush"},
-        "roofline": {"bound": "hbm", "kernel": f"{args.op} step", "achieved": round(achieved, 1), "peak": peak,
-                     "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None},
+        "roofline": {"bound": "hbm", "kernel": dom_key, "achieved": round(dom_achieved, 1), "peak": peak,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": round(dom_achieved / peak, 4),
+                     "traffic": None if traffic is None else int(traffic),
+                     "algorithmic_bytes": dom[2], "launches_per_step": dom[3]},
         "gpu_launches": w.launches * args.steps * world,
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
+    if traffic_src:
+        line["roofline"]["traffic_source"] = traffic_src
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = _op_cpu_baseline(args.op, w.bytes)
     return line

@@ -193,6 +193,41 @@ __device__ __forceinline__ float4 gather(const float* p, int row, int channels) 
 // values by a constant before sampling, so they receive no gradient.
 __device__ __forceinline__ float keep(float raw, float grad) { return fabsf(raw) <= 3.402823466e+38f ? grad : 0.0f; }
 
+// One item's sum over its samples: sum_k wa_k * value(row_k) for the lane's
+// slice, staging kChunk samples at a time. kSanitize reads a non-finite value
+// as 0. All lanes of the warp call it with the warp's common trip count.
+template <int G, bool kSanitize>
+__device__ __forceinline__ float4 sum_item(const Dims& d, const Map* maps, const float* off_item, const float* w_item,
+                                           float img_h, float img_w, int trips, int samples, int sub,
+                                           const float* vb, GroupSmem<G>& sm) {
+  using Sh = Shape<G>;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int s0 = 0; s0 < trips; s0 += Sh::kChunk) {
+    if (sub % Sh::kStager == 0) {
+      const int i = sub / Sh::kStager;
+      stage<G>(d, maps, off_item, w_item, img_h, img_w, s0 + i, samples, i, sm);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < Sh::kChunk; ++i) {
+      const int4 r4 = sm.row[i];
+      const float4 w4 = sm.wa[i];
+      const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+      const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 v = kSanitize ? gather(vb, rows[k], d.channels) : gather_raw(vb, rows[k], d.channels);
+        acc.x = fmaf(wa[k], v.x, acc.x);
+        acc.y = fmaf(wa[k], v.y, acc.y);
+        acc.z = fmaf(wa[k], v.z, acc.z);
+        acc.w = fmaf(wa[k], v.w, acc.w);
+      }
+    }
+    __syncwarp();
+  }
+  return acc;
+}
+
 template <int G>
 __global__ void __launch_bounds__(Shape<G>::kThreads) forward_kernel(Dims d, Grid grid, float eps,
                                                                      const float* __restrict__ value,
@@ -236,30 +271,16 @@ __global__ void __launch_bounds__(Shape<G>::kThreads) forward_kernel(Dims d, Gri
     const float* vb = value + b * d.cams * static_cast<int64_t>(d.stride_n) * d.channels + head * per_head + sub * 4;
     const float* off_item = offsets + it * block * 2;
     const float* w_item = weights + it * block;
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int s0 = 0; s0 < trips; s0 += Sh::kChunk) {
-      if (sub % Sh::kStager == 0) {
-        const int i = sub / Sh::kStager;
-        stage<G>(d, maps, off_item, w_item, img_h, img_w, s0 + i, samples, i, sm);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int i = 0; i < Sh::kChunk; ++i) {
-        const int4 r4 = sm.row[i];
-        const float4 w4 = sm.wa[i];
-        const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
-        const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float4 v = gather(vb, rows[k], d.channels);
-          acc.x = fmaf(wa[k], v.x, acc.x);
-          acc.y = fmaf(wa[k], v.y, acc.y);
-          acc.z = fmaf(wa[k], v.z, acc.z);
-          acc.w = fmaf(wa[k], v.w, acc.w);
-        }
-      }
-      __syncwarp();
-    }
+    // Gathers read raw values; a non-finite feature value (or an overflowing
+    // sum) leaves the lane's sum non-finite, and then every group of the warp
+    // (the staging syncs need the whole warp) sums its item again with each
+    // gathered value read as 0 when it is not finite, the reference's
+    // _sanitize_value. Finite inputs never pay for the test per value.
+    float4 acc = sum_item<G, false>(d, maps, off_item, w_item, img_h, img_w, trips, samples, sub, vb, sm);
+    const bool finite = fabsf(acc.x) <= 3.402823466e+38f && fabsf(acc.y) <= 3.402823466e+38f &&
+                        fabsf(acc.z) <= 3.402823466e+38f && fabsf(acc.w) <= 3.402823466e+38f;
+    if (__any_sync(0xffffffffu, live && !finite))
+      acc = sum_item<G, true>(d, maps, off_item, w_item, img_h, img_w, trips, samples, sub, vb, sm);
     if (live) {
       const float inv = visible > 0 ? __fdiv_rn(1.0f, static_cast<float>(visible)) : 0.0f;
       *reinterpret_cast<float4*>(out + cell * d.channels + head * per_head + sub * 4) =
@@ -334,11 +355,18 @@ __global__ void __launch_bounds__(Shape<G>::kThreads) backward_kernel(
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float4 raw = gather_raw(vb, rows[k], d.channels);
-          const float4 v = sanitize(raw);
-          t[i][k] = g.x * v.x + g.y * v.y + g.z * v.z + g.w * v.w;
+          float dot = g.x * raw.x + g.y * raw.y + g.z * raw.z + g.w * raw.w;
+          float4 pay = make_float4(wa[k] * g.x, wa[k] * g.y, wa[k] * g.z, wa[k] * g.w);
+          // the partial dot is finite unless a value of the slice is not (or a
+          // product overflows); only then are the values tested one by one
+          if (!(fabsf(dot) <= 3.402823466e+38f)) {
+            const float4 v = sanitize(raw);
+            dot = g.x * v.x + g.y * v.y + g.z * v.z + g.w * v.w;
+            pay = make_float4(keep(raw.x, pay.x), keep(raw.y, pay.y), keep(raw.z, pay.z), keep(raw.w, pay.w));
+          }
+          t[i][k] = dot;
           if (rows[k] >= 0)
-            msda::red_add_v4(gvb + static_cast<int64_t>(rows[k]) * d.channels, keep(raw.x, wa[k] * g.x),
-                             keep(raw.y, wa[k] * g.y), keep(raw.z, wa[k] * g.z), keep(raw.w, wa[k] * g.w));
+            msda::red_add_v4(gvb + static_cast<int64_t>(rows[k]) * d.channels, pay.x, pay.y, pay.z, pay.w);
         }
       }
       msda::reduce_to_stagers<G, C>(t, sub);
