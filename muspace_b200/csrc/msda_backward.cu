@@ -66,57 +66,6 @@ constexpr int kChunk = sizeof(T) == 2 ? 4 : MSDA_BWD_CHUNK_F32;
 template <typename T, int kBytes>
 constexpr int kMinBlocks = sizeof(T) == 2 ? (kBytes == 8 ? MSDA_BWD_MINBLOCKS_BF16 : 2) : MSDA_BWD_MINBLOCKS_F32;
 
-// Folds repeated corner rows of a chunk's kEnt staged (row, wa) entries into
-// their first occurrence: an entry whose row already appears at a lower
-// index adds its wa to that entry (shared-memory atomic) and its own wa
-// becomes 0, so a RED is due exactly for the entries with row >= 0 and
-// wa != 0. Rows are left as they are (the gathers still need them). Lane sub
-// of the group owns entries sub, sub + G, ...
-template <int G, int kEnt>
-__device__ __forceinline__ void fold_repeated_rows(const int* row, float* wa, int sub) {
-  static_assert(kEnt % 4 == 0, "entries come in whole samples");
-  constexpr int kPer = (kEnt + G - 1) / G;
-  int mine[kPer], target[kPer];
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = sub + j * G;
-    mine[j] = e < kEnt ? row[e] : -1;
-    target[j] = -1;
-  }
-  // earliest lower-index entry with the same row; only entries below
-  // (j + 1) * G can precede entry j, so the scan stops there
-#pragma unroll
-  for (int e4 = 0; e4 < ((kPer - 1) * G + G < kEnt ? (kPer - 1) * G + G : kEnt); e4 += 4) {
-    const int4 r4 = *reinterpret_cast<const int4*>(row + e4);
-    const int rs[4] = {r4.x, r4.y, r4.z, r4.w};
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e2 = e4 + u;
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        if (e2 >= (j + 1) * G) continue;  // never below entry j
-        const bool before = e2 < j * G || e2 < sub + j * G;
-        if (before && target[j] < 0 && rs[u] == mine[j] && mine[j] >= 0) target[j] = e2;
-      }
-    }
-  }
-  float moved[kPer];
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = sub + j * G;
-    moved[j] = (target[j] >= 0) ? wa[e] : 0.0f;
-  }
-  __syncwarp();  // every lane has read the wa it moves before any entry changes
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    if (target[j] >= 0) {
-      atomicAdd(wa + target[j], moved[j]);
-      wa[sub + j * G] = 0.0f;
-    }
-  }
-  __syncwarp();
-}
-
 // kScatter = false computes grad_loc / grad_w only; grad_value then comes from
 // the bucketed scatter kernel (msda_bucketed.cu).
 template <typename T, int G, int kBytes, int kStageMax, bool kScatter>
