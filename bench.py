@@ -393,49 +393,94 @@ def run_b200(args, cfg, dtype, rank, world, device):
     return line
 
 
-def run_e2e(args, local, dtype, inp, device, world, distributed):
-    """The same step through the C-ABI with host buffers: pinned H2D of the
-    inputs and D2H of the output and the three gradients, every step."""
+class E2ESlot:
+    """One set of device buffers of the end-to-end leg: ``inputs`` receive the
+    host copies, ``step()`` runs the op through the C-ABI, ``outputs`` go back."""
+
+    def __init__(self, inputs, outputs, step):
+        self.inputs, self.outputs, self.step = inputs, outputs, step
+
+
+def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device) -> float:
+    """Device time per step of ``steps`` end-to-end steps, each with the H2D
+    copy of its inputs from pinned host memory and the D2H copy of all its
+    outputs, double-buffered over ``slots`` (two sets of device buffers) on
+    three streams: the H2D of step i + 1 and the D2H of step i - 1 overlap the
+    compute of step i, and the two copy directions run concurrently (PCIe is
+    full duplex). A slot's inputs are rewritten only after its previous
+    compute, and its outputs only after their previous D2H. Max over ranks."""
     import torch.distributed as dist
 
-    host_in = {k: v.cpu().pin_memory() for k, v in inp.items() if k not in ("spatial_shapes", "level_start_index")}
-    dev_in = dict(inp)
-    step = Step(dev_in, dtype, device)
-    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (step.out, step.gv, step.gl, step.gw)]
-    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
-    steps = max(3, min(args.steps, 10))
+    s_in, s_comp, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
+    host_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in slot.outputs] for slot in slots]
+    in_done = [torch.cuda.Event() for _ in slots]
+    comp_done = [torch.cuda.Event() for _ in slots]
+    out_done = [torch.cuda.Event() for _ in slots]
 
-    def one():
-        for k, t in host_in.items():
-            dev_in[k].copy_(t, non_blocking=True)
-        step()
-        for dst, src in zip(host_out, (step.out, step.gv, step.gl, step.gw)):
-            dst.copy_(src, non_blocking=True)
+    def one(i):
+        j = i % len(slots)
+        slot = slots[j]
+        s_in.wait_event(comp_done[j])
+        with torch.cuda.stream(s_in):
+            for dst, src in zip(slot.inputs, host_in):
+                dst.copy_(src, non_blocking=True)
+        in_done[j].record(s_in)
+        s_comp.wait_event(in_done[j])
+        s_comp.wait_event(out_done[j])
+        with torch.cuda.stream(s_comp):
+            slot.step()
+        comp_done[j].record(s_comp)
+        s_out.wait_event(comp_done[j])
+        with torch.cuda.stream(s_out):
+            for dst, src in zip(host_out[j], slot.outputs):
+                dst.copy_(src, non_blocking=True)
+        out_done[j].record(s_out)
 
-    one()
-    torch.cuda.synchronize()
+    for i in range(len(slots)):  # warm-up: every slot once
+        one(i)
+    torch.cuda.synchronize(device)
     if distributed:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        one()
-    end.record()
-    torch.cuda.synchronize()
+    start.record(s_in)
+    for i in range(steps):
+        one(i)
+    main = torch.cuda.current_stream(device)
+    for s in (s_in, s_comp, s_out):
+        main.wait_stream(s)
+    end.record(main)
+    torch.cuda.synchronize(device)
     t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
     if distributed:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item()) / steps
+    return float(t.item()) / steps
+
+
+E2E_PATH = ("pinned host buffers -> cudaMemcpyAsync H2D -> {calls} (C-ABI) -> cudaMemcpyAsync D2H -> pinned host; "
+            "two device buffer sets, H2D / compute / D2H on three streams")
+
+
+def run_e2e(args, local, dtype, inp, device, world, distributed):
+    """The same step through the C-ABI with host buffers: pinned H2D of the
+    inputs and D2H of the output and the three gradients, every step."""
+    keys = [k for k in inp if k not in ("spatial_shapes", "level_start_index")]
+    host_in = [inp[k].cpu().pin_memory() for k in keys]
+    slots = []
+    for _ in range(2):
+        dev_in = {k: (v if k in ("spatial_shapes", "level_start_index") else v.clone()) for k, v in inp.items()}
+        step = Step(dev_in, dtype, device)
+        slots.append(E2ESlot([dev_in[k] for k in keys], [step.out, step.gv, step.gl, step.gw], step))
+    steps = max(3, min(args.steps, 10))
+    ms = pipelined_e2e(slots, host_in, steps, distributed, device)
     nbytes = cases.compulsory_bytes(local, dtype)["total"] * world
     return {
         "value": round(nbytes / (ms / 1e3) / 1e9, 3),
         "unit": "GB/s",
-        "h2d_bytes_per_step": h2d,
-        "d2h_bytes_per_step": d2h,
+        "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
+        "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in slots[0].outputs),
         "ms_per_step": round(ms, 3),
         "steps": steps,
-        "path": "pinned host buffers -> cudaMemcpyAsync -> ms_deform_attn_forward/backward (C-ABI) -> pinned host",
+        "path": E2E_PATH.format(calls="ms_deform_attn_forward/backward"),
     }
 
 
@@ -522,6 +567,7 @@ class OpWorkload:
                  _nbytes(mc, loc, w, grad, gmc, gl, gw), 1),
             ]
             self.dominant = ("backward", "deformable_aggregation_backward", 1)
+            self.calls = "deformable_aggregation_forward_opt/backward_opt"
             self.inputs, self.outputs = [mc, loc, w, grad], [out, gmc, gl, gw]
             self.workload = ("SparseDrive deformable aggregation fwd+bwd, reference production shapes: mc_ms_feat "
                              "[8, 89760, 256] fp32, 6 cams x 4 scales, 900 anchors x 13 pts, 8 groups, 40% in image")
@@ -553,6 +599,7 @@ class OpWorkload:
                  _nbytes(value, proj, offsets, weights, grad, gv, go, gwt), 1),
             ]
             self.dominant = ("backward", "flash_sca_backward", 1)
+            self.calls = "flash_bevpool_sca_forward/backward"
             self.inputs, self.outputs = [value, proj, offsets, weights, grad], [out, gv, go, gwt]
             self.workload = ("FlashSCA fwd+bwd, BEVFormer-base: 200x200x4 BEV grid, 6 cams, 4 levels of a 480x800 "
                              "image, 8 heads x 32 channels, 2 points per height, fp32")
@@ -576,6 +623,7 @@ class OpWorkload:
                            ("scatter", cameras, scatter_bytes, len(indexes))]
             # traffic is recorded per valid rebatched query of a camera launch
             self.dominant = ("scatter", "sca_scatter", valid)
+            self.calls = "ms_deform_attn_scatter_div_forward x 6 cameras"
             self.inputs, self.outputs = [inp["value"], loc, w, count], [slots]
             self.workload = ("BEVFormer-base SCA forward + rebatch scatter + count normalisation, 6 cameras x 10000 "
                              "rebatched queries (6000-10000 valid), 40000 BEV queries, 8 heads x 32 channels, bf16")
@@ -672,31 +720,15 @@ def run_op(args, rank, world, device):
     e2e = None
     if not args.no_e2e:
         host_in = [x.cpu().pin_memory() for x in w.inputs]
-        host_out = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in w.outputs]
-
-        def one():
-            for dst, src in zip(w.inputs, host_in):
-                dst.copy_(src, non_blocking=True)
-            w.step()
-            for dst, src in zip(host_out, w.outputs):
-                dst.copy_(src, non_blocking=True)
-
-        one()
-        torch.cuda.synchronize()
+        second = OpWorkload(args.op, device)  # the second device buffer set of the pipeline
+        slots = [E2ESlot(x.inputs, x.outputs, x.step) for x in (w, second)]
         steps = max(3, min(args.steps, 10))
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record()
-        for _ in range(steps):
-            one()
-        e2.record()
-        torch.cuda.synchronize()
-        t2 = torch.tensor([s2.elapsed_time(e2)], dtype=torch.float64, device=device)
-        if world > 1:
-            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t2.item()) / steps
+        e2e_ms = pipelined_e2e(slots, host_in, steps, world > 1, device)
         e2e = {"value": round(w.bytes * world / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": _nbytes(*host_in), "d2h_bytes_per_step": _nbytes(*host_out),
-               "ms_per_step": round(e2e_ms, 3), "steps": steps}
+               "h2d_bytes_per_step": _nbytes(*host_in), "d2h_bytes_per_step": _nbytes(*w.outputs),
+               "ms_per_step": round(e2e_ms, 3), "steps": steps,
+               "path": E2E_PATH.format(calls=w.calls)}
+        del second, slots
     if rank != 0:
         return None
     peak, peak_src = _peaks()

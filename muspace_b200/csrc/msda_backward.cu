@@ -44,10 +44,10 @@ namespace msda {
 #define MSDA_BWD_CHUNK_F32 2
 #endif
 #ifndef MSDA_BWD_MINBLOCKS_F32
-#define MSDA_BWD_MINBLOCKS_F32 3
+#define MSDA_BWD_MINBLOCKS_F32 4
 #endif
 #ifndef MSDA_BWD_MINBLOCKS_BF16
-#define MSDA_BWD_MINBLOCKS_BF16 3
+#define MSDA_BWD_MINBLOCKS_BF16 4
 #endif
 #ifndef MSDA_BWD_PAIR
 #define MSDA_BWD_PAIR 1
@@ -60,7 +60,8 @@ namespace msda {
 #endif
 // Samples per dot round (their partial dots live in registers: 4 per sample)
 // and CTAs per SM the register budget is sized for; measured on B200 (fp32
-// D = 32: rounds of 2 at 3 CTAs/SM beat rounds of 4 at 2 or 3).
+// D = 32: rounds of 2 at 3 CTAs/SM beat rounds of 4 at 2 or 3; 4 CTAs/SM at
+// 64 registers beat 3 for fp32 D = 32 and bf16 8-byte lanes by 2-3 %).
 template <typename T>
 constexpr int kChunk = sizeof(T) == 2 ? 4 : MSDA_BWD_CHUNK_F32;
 template <typename T, int kBytes>
@@ -210,14 +211,21 @@ struct PairShape {
   static constexpr int G = kChannels / 4;                          // lanes per head-row
   static constexpr int kPairs16 = kPer16 / 2;                      // fp32 pairs per chunk
 #ifndef MSDA_PAIR_CORNERS
-#define MSDA_PAIR_CORNERS 2
+#define MSDA_PAIR_CORNERS 1
 #endif
-  // corner gathers issued together (register budget: kCPL * 4 words each)
+  // corner gathers issued together (register budget: kCPL * 4 words each; at
+  // 64 registers one corner at a time measured fastest for D = 32)
   static constexpr int kCornersInFlight = kCPL == 1 ? 4 : (kCPL == 2 ? MSDA_PAIR_CORNERS : 1);
 };
 
+// CTAs per SM the lane-pair kernel's register budget is sized for (4: 64
+// registers, 32 resident warps; 8.60 -> 8.06 ms for the c4 backward against 3).
+#ifndef MSDA_PAIR_MINBLOCKS
+#define MSDA_PAIR_MINBLOCKS 4
+#endif
+
 template <typename T, int kCPL, int kStageMax, bool kScatter>
-__global__ void __launch_bounds__(kCtaThreads, 3) backward_pair_kernel(
+__global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pair_kernel(
     Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
     const T* __restrict__ loc, const T* __restrict__ weight, const T* __restrict__ grad_out,
     float* __restrict__ grad_value, float* __restrict__ grad_loc, float* __restrict__ grad_weight,
