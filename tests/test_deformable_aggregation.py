@@ -237,3 +237,18 @@ def test_production_shapes_opt_equals_base(cuda_device):
     torch.testing.assert_close(opt[0], base[0], rtol=1e-4, atol=1e-4)
     for a, b in zip(opt[1:], base[1:]):
         torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pts,cams,channels,groups", [(40, 3, 64, 4), (13, 1, 512, 8), (5, 7, 32, 2)])
+def test_point_camera_and_channel_extents_match_the_oracle(cuda_device, pts, cams, channels, groups):
+    """More than 32 points per camera (two compaction rounds per camera-major
+    warp), a single camera, 512 channels (four lane rounds) and 7 cameras."""
+    t, grad = cases.deformable_aggregation_inputs(cuda_device, batch=2, anchors=24, pts=pts, cams=cams,
+                                                  channels=channels, groups=groups, active=0.6, seed=7)
+    got = _c_abi(t, grad, optimized=True)
+    torch.cuda.synchronize()
+    expected = deformable_aggregation_forward_backward(*[x.cpu() for x in t], grad.cpu())
+    torch.testing.assert_close(got[0].cpu(), expected[0], rtol=1e-4, atol=1e-4)
+    for value, ref in zip(got[1:], expected[1:]):
+        torch.testing.assert_close(value.cpu(), ref, rtol=1e-3, atol=1e-3)

@@ -143,3 +143,23 @@ def test_bevformer_like_case_matches_the_oracle(cuda_device):
     torch.testing.assert_close(out.detach().cpu(), exp[0], rtol=1e-4, atol=1e-4)
     for leaf, ref in zip((leaves[0], leaves[5], leaves[6]), exp[1:]):
         torch.testing.assert_close(leaf.grad.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+def test_more_landing_pairs_than_a_warp_matches_the_oracle(cuda_device):
+    """6 cameras x 8 heights = 48 (camera, height) pairs per cell: the
+    projection takes several rounds of the lane group, and the backward's
+    level-major chunks mix pairs of several rounds."""
+    t, kw = bevformer_inputs(cuda_device, grid=(12, 12, 8), points=2, seed=11)
+    leaves = list(t)
+    for i in (0, 5, 6):
+        leaves[i] = t[i].clone().requires_grad_(True)
+    out = flash_bevpool_sca(*leaves, **kw)
+    grad = torch.randn(out.shape, generator=torch.Generator().manual_seed(2)).to(cuda_device)
+    out.backward(grad)
+    exp = flash_sca_forward_backward(*[x.cpu() for x in t], kw["grid_size"], kw["voxel_size"], kw["voxel_min"],
+                                     grad.cpu())
+    assert out.abs().sum() > 0
+    torch.testing.assert_close(out.detach().cpu(), exp[0], rtol=1e-4, atol=1e-4)
+    for leaf, ref in zip((leaves[0], leaves[5], leaves[6]), exp[1:]):
+        torch.testing.assert_close(leaf.grad.cpu(), ref, rtol=1e-3, atol=1e-3)
