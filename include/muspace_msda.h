@@ -32,6 +32,7 @@
 #ifndef MUSPACE_MSDA_H_
 #define MUSPACE_MSDA_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -185,6 +186,43 @@ MSDA_API int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t 
                                           const void *sampling_locations, const void *attention_weights,
                                           const void *grad_output, float *grad_value, float *grad_sampling_loc,
                                           float *grad_attn_weight, void *stream);
+
+/*
+ * Deterministic backward (no counterpart in the reference, whose atomicAdd
+ * backward is not reproducible either): the same arguments and results as
+ * ms_deform_attn_backward / msda_backward, but grad_value is bit-identical
+ * from run to run. Contributions to grad_value are summed as 64-bit fixed-point
+ * integers (associative, so the order of the additions no longer matters) at a
+ * power-of-two scale taken on the device from max |grad_output| and
+ * max |attention_weights|, converted back once and added into grad_value;
+ * grad_sampling_loc / grad_attn_weight come from the same kernels as the
+ * default path, which are already reproducible. The result equals the exactly
+ * rounded sum of the fp32 contributions, each kept to 2^-(61 - k) of the
+ * largest possible one, k = ceil(log2(Lq * L * P)) + 1. With a non-finite value
+ * in grad_output or attention_weights, grad_value receives fp32 atomic
+ * additions instead (not reproducible in its finite elements).
+ *
+ * The caller provides the work space: `workspace` of at least
+ * msda_deterministic_workspace_bytes bytes (256 + 8 * B * Lin * Hh * D),
+ * 256-byte aligned, uint8 for the DLPack form. The call clears it itself. Calls
+ * that share a work space must be ordered on the GPU.
+ */
+MSDA_API int msda_deterministic_workspace_bytes(const msda_dims_t *dims, size_t *bytes);
+
+MSDA_API int ms_deform_attn_backward_deterministic(const DLTensor *value, const DLTensor *spatial_shapes,
+                                                   const DLTensor *level_start_index,
+                                                   const DLTensor *sampling_locations,
+                                                   const DLTensor *attention_weights, const DLTensor *grad_output,
+                                                   DLTensor *grad_value, DLTensor *grad_sampling_loc,
+                                                   DLTensor *grad_attn_weight, DLTensor *workspace, int im2col_step,
+                                                   void *stream);
+
+MSDA_API int msda_backward_deterministic(msda_dtype_t dtype, const msda_dims_t *dims, const void *value,
+                                         const int64_t *spatial_shapes, const int64_t *level_start_index,
+                                         const void *sampling_locations, const void *attention_weights,
+                                         const void *grad_output, float *grad_value, float *grad_sampling_loc,
+                                         float *grad_attn_weight, void *workspace, size_t workspace_bytes,
+                                         void *stream);
 
 /*
  * BEVFormer spatial cross-attention, forward fused with the rebatch scatter

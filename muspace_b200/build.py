@@ -21,8 +21,8 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 INCLUDE = PACKAGE.parent / "include"
 LIBRARY = PACKAGE / "native" / "libmuspace_ops.so"
-SOURCES = ("msda_capi.cpp", "msda_forward.cu", "msda_backward.cu", "msda_bucketed.cu", "msda_noalloc.cu", "deform_agg.cu",
-           "flash_sca.cu")
+SOURCES = ("msda_capi.cpp", "msda_forward.cu", "msda_backward.cu", "msda_bucketed.cu", "msda_noalloc.cu",
+           "msda_deterministic.cu", "deform_agg.cu", "flash_sca.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

@@ -425,10 +425,12 @@ __global__ void __launch_bounds__(256) backward_scalar_kernel(Dims d, const T* _
             part_w = fmaf(gc, bil, part_w);
             part_x = fmaf(gc, c.hh * (v[1] - v[0]) + c.lh * (v[3] - v[2]), part_x);
             part_y = fmaf(gc, c.hw * (v[2] - v[0]) + c.lw * (v[3] - v[1]), part_y);
+            if (grad_value != nullptr) {  // null: grad_loc / grad_w only
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (c.row[k] >= 0)
-                atomicAdd(grad_value + vrow0 + static_cast<int64_t>(c.row[k]) * row_stride + ch, c.w[k] * a * gc);
+              for (int k = 0; k < 4; ++k)
+                if (c.row[k] >= 0)
+                  atomicAdd(grad_value + vrow0 + static_cast<int64_t>(c.row[k]) * row_stride + ch, c.w[k] * a * gc);
+            }
           }
         }
         grad_weight[so] = part_w;
@@ -517,13 +519,13 @@ static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t 
   } else {
     if (const int g = vec_lanes(d.channels, sizeof(T), 16, a)) return launch_backward_lanes<T, 16>(g, d, a, stream);
   }
-  if (a.skip_grad_value) return cudaErrorInvalidValue;  // the scalar kernel always scatters
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int64_t blocks = (items + kCtaThreads - 1) / kCtaThreads;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
   backward_scalar_kernel<T><<<grid, kCtaThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
-      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight);
+      static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.skip_grad_value ? nullptr : a.grad_value,
+      a.grad_loc, a.grad_weight);
   return cudaGetLastError();
 }
 

@@ -296,6 +296,104 @@ int msda_backward(msda_dtype_t dtype, const msda_dims_t* dims, const void* value
   });
 }
 
+int msda_deterministic_workspace_bytes(const msda_dims_t* dims, size_t* bytes) {
+  return guarded([&] {
+    require(dims != nullptr && bytes != nullptr, "dims or bytes is null");
+    check_dims(*dims);
+    *bytes = msda::deterministic_workspace_bytes(to_kernel_dims(*dims));
+  });
+}
+
+int ms_deform_attn_backward_deterministic(const DLTensor* value, const DLTensor* spatial_shapes,
+                                          const DLTensor* level_start_index, const DLTensor* sampling_locations,
+                                          const DLTensor* attention_weights, const DLTensor* grad_output,
+                                          DLTensor* grad_value, DLTensor* grad_sampling_loc,
+                                          DLTensor* grad_attn_weight, DLTensor* workspace, int im2col_step,
+                                          void* stream) {
+  return guarded([&] {
+    const msda::DType dt = storage_dtype(value);
+    const uint8_t code = dt == msda::DType::kBF16 ? kDLBfloat : kDLFloat;
+    const uint8_t bits = dt == msda::DType::kBF16 ? 16 : 32;
+    const int dev = value->device.device_id;
+    check_tensor(value, "value", code, bits, 4, dev);
+    check_tensor(spatial_shapes, "spatial_shapes", kDLInt, 64, 2, dev);
+    check_tensor(level_start_index, "level_start_index", kDLInt, 64, 1, dev);
+    check_tensor(sampling_locations, "sampling_locations", code, bits, 6, dev);
+    check_tensor(attention_weights, "attention_weights", code, bits, 5, dev);
+    check_tensor(grad_output, "grad", code, bits, 3, dev);
+    check_tensor(grad_value, "grad_value", kDLFloat, 32, 4, dev);
+    check_tensor(grad_sampling_loc, "grad_sampling_locations", kDLFloat, 32, 6, dev);
+    check_tensor(grad_attn_weight, "grad_attention_weights", kDLFloat, 32, 5, dev);
+    check_tensor(workspace, "workspace", kDLUInt, 8, 1, dev);
+    const msda_dims_t d =
+        dims_from_views(value, spatial_shapes, level_start_index, sampling_locations, attention_weights, im2col_step);
+    require(grad_output->shape[0] == d.batch && grad_output->shape[1] == d.queries &&
+                grad_output->shape[2] == d.heads * d.channels,
+            "grad must have shape (B, Lq, Hh * D)");
+    for (int i = 0; i < 4; ++i)
+      require(grad_value->shape[i] == value->shape[i], "grad_value must have the shape of value");
+    for (int i = 0; i < 6; ++i)
+      require(grad_sampling_loc->shape[i] == sampling_locations->shape[i],
+              "grad_sampling_locations must have the shape of sampling_locations");
+    for (int i = 0; i < 5; ++i)
+      require(grad_attn_weight->shape[i] == attention_weights->shape[i],
+              "grad_attention_weights must have the shape of attention_weights");
+    const msda::Dims kd = to_kernel_dims(d);
+    const size_t need = msda::deterministic_workspace_bytes(kd);
+    require(static_cast<size_t>(workspace->shape[0]) >= need,
+            "workspace holds " + std::to_string(workspace->shape[0]) + " bytes, the call needs " +
+                std::to_string(need) + " (msda_deterministic_workspace_bytes)");
+    require((reinterpret_cast<uintptr_t>(data_of(workspace)) & 255u) == 0, "workspace must be 256-byte aligned");
+    DeviceGuard guard(dev);
+    msda::Args a{};
+    a.value = data_of(value);
+    a.shapes = static_cast<const int64_t*>(data_of(spatial_shapes));
+    a.starts = static_cast<const int64_t*>(data_of(level_start_index));
+    a.loc = data_of(sampling_locations);
+    a.weight = data_of(attention_weights);
+    a.grad_out = data_of(grad_output);
+    a.grad_value = static_cast<float*>(data_of(grad_value));
+    a.grad_loc = static_cast<float*>(data_of(grad_sampling_loc));
+    a.grad_weight = static_cast<float*>(data_of(grad_attn_weight));
+    check_launch(msda::launch_backward_deterministic(dt, kd, a, data_of(workspace), static_cast<cudaStream_t>(stream)),
+                 "ms_deform_attn_backward_deterministic");
+  });
+}
+
+int msda_backward_deterministic(msda_dtype_t dtype, const msda_dims_t* dims, const void* value,
+                                const int64_t* spatial_shapes, const int64_t* level_start_index,
+                                const void* sampling_locations, const void* attention_weights,
+                                const void* grad_output, float* grad_value, float* grad_sampling_loc,
+                                float* grad_attn_weight, void* workspace, size_t workspace_bytes, void* stream) {
+  return guarded([&] {
+    require(dtype == MSDA_DTYPE_FLOAT32 || dtype == MSDA_DTYPE_BFLOAT16, "dtype must be float32 or bfloat16");
+    require(dims != nullptr, "dims is null");
+    check_dims(*dims);
+    const bool empty = dims->batch * dims->queries * dims->heads == 0;
+    require(empty || (value && spatial_shapes && level_start_index && sampling_locations && attention_weights &&
+                      grad_output && grad_value && grad_sampling_loc && grad_attn_weight && workspace),
+            "a required pointer is null");
+    const msda::Dims kd = to_kernel_dims(*dims);
+    const size_t need = msda::deterministic_workspace_bytes(kd);
+    require(empty || workspace_bytes >= need,
+            "workspace holds " + std::to_string(workspace_bytes) + " bytes, the call needs " + std::to_string(need));
+    require(empty || (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, "workspace must be 256-byte aligned");
+    msda::Args a{};
+    a.value = value;
+    a.shapes = spatial_shapes;
+    a.starts = level_start_index;
+    a.loc = sampling_locations;
+    a.weight = attention_weights;
+    a.grad_out = grad_output;
+    a.grad_value = grad_value;
+    a.grad_loc = grad_sampling_loc;
+    a.grad_weight = grad_attn_weight;
+    const msda::DType dt = dtype == MSDA_DTYPE_BFLOAT16 ? msda::DType::kBF16 : msda::DType::kF32;
+    check_launch(msda::launch_backward_deterministic(dt, kd, a, workspace, static_cast<cudaStream_t>(stream)),
+                 "msda_backward_deterministic");
+  });
+}
+
 int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t* dims, const void* value,
                                  const int64_t* spatial_shapes, const int64_t* level_start_index,
                                  const void* sampling_locations, const void* attention_weights,

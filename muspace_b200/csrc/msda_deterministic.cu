@@ -1,0 +1,176 @@
+// Deterministic MSDA backward: grad_value summed in 64-bit fixed point.
+//
+// The default backward adds every sample's corner contributions w_k * a * g
+// into the fp32 grad_value with vector REDs, so the order of the additions,
+// and with it the last bits of grad_value, changes from run to run (the
+// reference's atomicAdd kernels behave the same). This path makes grad_value
+// bit-reproducible with integer arithmetic instead of a destination sort:
+//   0. one pass takes max |grad_output| and max |attention_weights|, which
+//      bound every contribution (w_k <= 1);
+//   1. the row-wise backward writes grad_loc / grad_w (each by one lane, in a
+//      fixed order, as in the default path) without touching grad_value;
+//   2. every contribution, converted to a 64-bit integer at a power-of-two
+//      scale derived from that bound, is added into a 64-bit accumulator per
+//      grad_value element; integer addition is associative, so the sums do not
+//      depend on the order in which the additions land;
+//   3. each accumulator is converted back once and added into grad_value.
+// The scale leaves headroom for every sample of a (batch, head) landing on one
+// element, so no sum can overflow. A contribution is kept to 2^-(61 - headroom)
+// of the bound, finer than fp32 resolution for all but contributions far below
+// the largest one; the result is the exactly rounded sum of the fp32
+// contributions to that resolution. When grad_output or the weights hold a
+// non-finite value, step 2 adds the fp32 contributions into grad_value
+// directly (the non-finite elements are the same in any order).
+#include "msda_device.cuh"
+
+namespace msda {
+namespace {
+
+constexpr size_t kHeaderBytes = 256;  // two words of maxima, padded to keep the accumulators aligned
+
+// Largest |x| of two tensors as float bits (for x >= 0 the unsigned order of
+// the bits is the float order, with NaN above inf).
+template <typename T>
+__global__ void __launch_bounds__(256) max_abs_kernel(const T* __restrict__ g, int64_t ng, const T* __restrict__ w,
+                                                     int64_t nw, unsigned* __restrict__ header) {
+  unsigned mg = 0u, mw = 0u;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < ng; i += stride)
+    mg = max(mg, __float_as_uint(fabsf(to_f32(g[i]))));
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nw; i += stride)
+    mw = max(mw, __float_as_uint(fabsf(to_f32(w[i]))));
+  mg = __reduce_max_sync(0xffffffffu, mg);
+  mw = __reduce_max_sync(0xffffffffu, mw);
+  if (threadIdx.x % 32 == 0) {
+    atomicMax(header, mg);
+    atomicMax(header + 1, mw);
+  }
+}
+
+struct FixedPoint {
+  bool finite;
+  double scale;
+};
+
+// The scale of step 2: contributions are bounded by s = max|g| * max|a|, and
+// s * scale < 2^(62 - headroom_bits) (frexp: s < 2^e).
+__device__ __forceinline__ FixedPoint fixed_point(const unsigned* header, int headroom_bits) {
+  const float mg = __uint_as_float(header[0]), mw = __uint_as_float(header[1]);
+  FixedPoint f;
+  f.finite = isfinite(mg) && isfinite(mw);
+  const double s = static_cast<double>(mg) * static_cast<double>(mw);
+  int e = 0;
+  frexp(s, &e);
+  f.scale = s > 0.0 ? ldexp(1.0, 62 - headroom_bits - e) : 1.0;
+  return f;
+}
+
+// Step 2: one warp per head-row (b, q, h), lanes over its channels.
+template <typename T>
+__global__ void __launch_bounds__(256) fixed_point_scatter_kernel(
+    Dims d, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts, const T* __restrict__ loc,
+    const T* __restrict__ weight, const T* __restrict__ grad_out, const unsigned* __restrict__ header,
+    int headroom_bits, unsigned long long* __restrict__ acc, float* __restrict__ grad_value) {
+  extern __shared__ Level levels[];
+  stage_levels(levels, shapes, starts, d);
+  const FixedPoint fp = fixed_point(header, headroom_bits);
+  const int lane = threadIdx.x % 32;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int64_t row_stride = static_cast<int64_t>(d.heads) * d.channels;
+  const int samples = d.levels * d.points;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32; item < items;
+       item += warps) {
+    const int h = static_cast<int>(item % d.heads);
+    const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
+    const int64_t head0 = b * d.spatial_size * row_stride + static_cast<int64_t>(h) * d.channels;
+    for (int c0 = lane; c0 < d.channels; c0 += 32) {
+      const float gc = to_f32(grad_out[item * d.channels + c0]);
+      for (int s = 0; s < samples; ++s) {
+        const int64_t so = item * samples + s;
+        const float2 xy = load_loc(loc + 2 * so);
+        const float a = to_f32(weight[so]);
+        Corners c;
+        if (!corners(levels[s / d.points], xy.x, xy.y, c)) continue;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (c.row[k] < 0) continue;
+          const float contribution = c.w[k] * a * gc;
+          const int64_t at = head0 + static_cast<int64_t>(c.row[k]) * row_stride + c0;
+          if (fp.finite)
+            atomicAdd(acc + at, static_cast<unsigned long long>(
+                                    __double2ll_rn(static_cast<double>(contribution) * fp.scale)));
+          else
+            atomicAdd(grad_value + at, contribution);
+        }
+      }
+    }
+  }
+}
+
+// Step 3: grad_value += acc / scale, one writer per element.
+__global__ void __launch_bounds__(256) fixed_point_finish_kernel(int64_t n, const unsigned long long* __restrict__ acc,
+                                                                 const unsigned* __restrict__ header,
+                                                                 int headroom_bits, float* __restrict__ grad_value) {
+  const FixedPoint fp = fixed_point(header, headroom_bits);
+  if (!fp.finite) return;
+  const double inv = 1.0 / fp.scale;  // a power of two: exact
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    grad_value[i] += static_cast<float>(static_cast<double>(static_cast<long long>(acc[i])) * inv);
+}
+
+int grid_for(int64_t threads) {
+  const int64_t blocks = (threads + 255) / 256;
+  return static_cast<int>(blocks < 148 * 64 ? (blocks > 0 ? blocks : 1) : 148 * 64);
+}
+
+// Most contributions one grad_value element can receive: every sample of a
+// (batch, head) landing on it (a sample's four corners are distinct pixels).
+int headroom_bits(const Dims& d) {
+  const int64_t most = static_cast<int64_t>(d.queries) * d.levels * d.points;
+  int bits = 1;
+  while (bits < 62 && (int64_t{1} << bits) < most) ++bits;
+  return bits + 1;
+}
+
+template <typename T>
+cudaError_t launch_t(const Dims& d, const Args& a, void* workspace, cudaStream_t stream) {
+  const int64_t n_value = static_cast<int64_t>(d.batch) * d.spatial_size * d.heads * d.channels;
+  auto* header = static_cast<unsigned*>(workspace);
+  auto* acc = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(workspace) + kHeaderBytes);
+  cudaError_t err = cudaMemsetAsync(workspace, 0, deterministic_workspace_bytes(d), stream);
+  if (err != cudaSuccess) return err;
+  const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
+  const int64_t n_grad = items * d.channels;
+  const int64_t n_weight = items * d.levels * d.points;
+  max_abs_kernel<T><<<grid_for(n_grad > n_weight ? n_grad : n_weight), 256, 0, stream>>>(
+      static_cast<const T*>(a.grad_out), n_grad, static_cast<const T*>(a.weight), n_weight, header);
+  if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  Args dots = a;
+  dots.skip_grad_value = true;
+  if ((err = launch_backward_rowwise(sizeof(T) == 2 ? DType::kBF16 : DType::kF32, d, dots, stream)) != cudaSuccess)
+    return err;
+  const int bits = headroom_bits(d);
+  fixed_point_scatter_kernel<T><<<grid_for(items * 32), 256, level_smem(d), stream>>>(
+      d, a.shapes, a.starts, static_cast<const T*>(a.loc), static_cast<const T*>(a.weight),
+      static_cast<const T*>(a.grad_out), header, bits, acc, a.grad_value);
+  if ((err = cudaGetLastError()) != cudaSuccess) return err;
+  fixed_point_finish_kernel<<<grid_for(n_value), 256, 0, stream>>>(n_value, acc, header, bits, a.grad_value);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t deterministic_workspace_bytes(const Dims& d) {
+  return kHeaderBytes + static_cast<size_t>(d.batch) * d.spatial_size * d.heads * d.channels * sizeof(uint64_t);
+}
+
+cudaError_t launch_backward_deterministic(DType dtype, const Dims& d, const Args& a, void* workspace,
+                                          cudaStream_t stream) {
+  if (d.batch == 0 || d.queries == 0 || d.heads == 0 || d.channels == 0) return cudaSuccess;
+  return dtype == DType::kBF16 ? launch_t<__nv_bfloat16>(d, a, workspace, stream)
+                               : launch_t<float>(d, a, workspace, stream);
+}
+
+}  // namespace msda

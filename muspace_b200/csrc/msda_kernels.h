@@ -78,8 +78,8 @@ inline int vec_lanes(int channels, size_t elem, size_t lane_bytes, const Args& a
 // Lanes per head-row for the 16-byte vector kernels (forward, bucketed scatter).
 inline int vec_group(int channels, size_t elem, const Args& a) { return vec_lanes(channels, elem, 16, a); }
 
-// Entry points used by the C-ABI: pick the tiled path when it applies and
-// fall back to the row-wise kernels otherwise (msda_tiled.cu).
+// Entry points used by the C-ABI (msda_bucketed.cu): the row-wise kernels, or
+// the bucketed backward in builds with MSDA_BUCKETED_BACKWARD=1.
 cudaError_t launch_forward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 
@@ -88,6 +88,13 @@ cudaError_t launch_backward(DType dtype, const Dims& d, const Args& a, cudaStrea
 // and the scratch-free row-wise kernels run instead), and the launch itself.
 size_t backward_scratch_bytes(DType dtype, const Dims& d, const Args& a);
 cudaError_t launch_backward_on_scratch(DType dtype, const Dims& d, const Args& a, void* scratch, cudaStream_t stream);
+
+// Deterministic backward (msda_deterministic.cu): grad_value summed in 64-bit
+// fixed point on a caller-provided workspace of deterministic_workspace_bytes
+// (256-byte aligned), grad_loc / grad_w from the row-wise kernels.
+size_t deterministic_workspace_bytes(const Dims& d);
+cudaError_t launch_backward_deterministic(DType dtype, const Dims& d, const Args& a, void* workspace,
+                                          cudaStream_t stream);
 
 // The fixed per-device scratch array (msda_noalloc.cu).
 size_t static_scratch_capacity();

@@ -74,6 +74,16 @@ def _requires_native_backend(
     )
 
 
+def deterministic_workspace_bytes(value: torch.Tensor, sampling_locations: torch.Tensor) -> int:
+    """Work space of the deterministic backward for these views, as the
+    library computes it (``msda_deterministic_workspace_bytes``)."""
+    from ..runtime.native import deterministic_workspace_bytes as query
+
+    batch, spatial, heads, channels = value.shape
+    _, queries, _, levels, points, _ = sampling_locations.shape
+    return query(batch, spatial, heads, channels, levels, queries, points)
+
+
 class _NativeMSDAFunction(torch.autograd.Function):
     """Autograd over the two C-ABI calls (reference ``ops/...:101-190``).
 
@@ -81,7 +91,9 @@ class _NativeMSDAFunction(torch.autograd.Function):
     from fp32 storage and cast back. The backward hands the kernel fp32
     gradient buffers: ``grad_value`` zero-filled (the kernel accumulates into
     it), ``grad_sampling`` / ``grad_attention`` uninitialised because the
-    kernel writes every element of them.
+    kernel writes every element of them. Under
+    ``torch.use_deterministic_algorithms(True)`` the backward runs the
+    deterministic entry point (bit-identical ``grad_value`` from run to run).
     """
 
     @staticmethod
@@ -128,18 +140,15 @@ class _NativeMSDAFunction(torch.autograd.Function):
         grad_sampling = torch.empty_like(sampling_locations, dtype=torch.float32)
         grad_attention = torch.empty_like(attention_weights, dtype=torch.float32)
         grad_output = grad_output.to(dtype=value.dtype).contiguous()
-        ext.ms_deform_attn_backward(
-            value,
-            spatial_shapes,
-            level_start_index,
-            sampling_locations,
-            attention_weights,
-            grad_output,
-            grad_value,
-            grad_sampling,
-            grad_attention,
-            ctx.im2col_step,
-        )
+        args = (value, spatial_shapes, level_start_index, sampling_locations, attention_weights, grad_output,
+                grad_value, grad_sampling, grad_attention)
+        if torch.are_deterministic_algorithms_enabled():
+            # reproducible grad_value: 64-bit fixed-point sums on a work space
+            workspace = torch.empty(deterministic_workspace_bytes(value, sampling_locations), dtype=torch.uint8,
+                                    device=value.device)
+            ext.ms_deform_attn_backward_deterministic(*args, workspace, ctx.im2col_step)
+        else:
+            ext.ms_deform_attn_backward(*args, ctx.im2col_step)
         return (
             grad_value.to(dtype=ctx.value_dtype),
             None,

@@ -124,6 +124,7 @@ def _stream_of(tensors) -> int:
 _SIGNATURES: dict[str, tuple[str, ...]] = {
     "ms_deform_attn_forward": ("t",) * 6 + ("i",),
     "ms_deform_attn_backward": ("t",) * 9 + ("i",),
+    "ms_deform_attn_backward_deterministic": ("t",) * 10 + ("i",),
     "ms_deform_attn_scatter_div_forward": ("t",) * 8 + ("i",),
     "deformable_aggregation_forward_opt": ("t",) * 6,
     "deformable_aggregation_forward_base": ("t",) * 6,
@@ -215,6 +216,28 @@ def native_function(name: str) -> Callable[..., Any]:
         return module.get_function(name)
     except (AttributeError, KeyError) as exc:
         raise NativeModuleUnavailable(f"muSPACE-B200 native library does not export {name!r}") from exc
+
+
+class MsdaDims(ctypes.Structure):
+    """``msda_dims_t`` of include/muspace_msda.h."""
+
+    _fields_ = [(name, ctypes.c_int64) for name in
+                ("batch", "spatial_size", "heads", "channels", "levels", "queries", "points")]
+
+
+def deterministic_workspace_bytes(batch: int, spatial_size: int, heads: int, channels: int, levels: int,
+                                  queries: int, points: int) -> int:
+    """``msda_deterministic_workspace_bytes``: device bytes the deterministic
+    backward needs for these sizes."""
+    module = load_native_module()
+    fn = module.lib.msda_deterministic_workspace_bytes
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.POINTER(MsdaDims), ctypes.POINTER(ctypes.c_size_t)]
+    dims = MsdaDims(batch, spatial_size, heads, channels, levels, queries, points)
+    out = ctypes.c_size_t(0)
+    if fn(ctypes.byref(dims), ctypes.byref(out)) != 0:
+        raise RuntimeError(f"msda_deterministic_workspace_bytes: {module.last_error()}")
+    return int(out.value)
 
 
 class NativeModuleProxy:
