@@ -65,7 +65,9 @@ __device__ __forceinline__ FixedPoint fixed_point(const unsigned* header, int he
   return f;
 }
 
-// Step 2: one warp per head-row (b, q, h), lanes over its channels.
+// Step 2: one warp per head-row (b, q, h). Lane i computes the geometry of
+// sample s0 + i once; the warp then walks the samples, broadcasting each
+// one's corner rows and w_k * a, with lanes over the channels.
 template <typename T>
 __global__ void __launch_bounds__(256) fixed_point_scatter_kernel(
     Dims d, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts, const T* __restrict__ loc,
@@ -84,24 +86,41 @@ __global__ void __launch_bounds__(256) fixed_point_scatter_kernel(
     const int h = static_cast<int>(item % d.heads);
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
     const int64_t head0 = b * d.spatial_size * row_stride + static_cast<int64_t>(h) * d.channels;
-    for (int c0 = lane; c0 < d.channels; c0 += 32) {
-      const float gc = to_f32(grad_out[item * d.channels + c0]);
-      for (int s = 0; s < samples; ++s) {
-        const int64_t so = item * samples + s;
+    for (int s0 = 0; s0 < samples; s0 += 32) {
+      int row[4] = {-1, -1, -1, -1};
+      float wa[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (s0 + lane < samples) {
+        const int64_t so = item * samples + s0 + lane;
         const float2 xy = load_loc(loc + 2 * so);
         const float a = to_f32(weight[so]);
         Corners c;
-        if (!corners(levels[s / d.points], xy.x, xy.y, c)) continue;
+        if (corners(levels[(s0 + lane) / d.points], xy.x, xy.y, c)) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (c.row[k] < 0) continue;
-          const float contribution = c.w[k] * a * gc;
-          const int64_t at = head0 + static_cast<int64_t>(c.row[k]) * row_stride + c0;
-          if (fp.finite)
-            atomicAdd(acc + at, static_cast<unsigned long long>(
-                                    __double2ll_rn(static_cast<double>(contribution) * fp.scale)));
-          else
-            atomicAdd(grad_value + at, contribution);
+          for (int k = 0; k < 4; ++k) {
+            row[k] = c.row[k];
+            wa[k] = c.w[k] * a;
+          }
+        }
+      }
+      const int n = samples - s0 < 32 ? samples - s0 : 32;
+      for (int c0 = 0; c0 < d.channels; c0 += 32) {
+        const int ch = c0 + lane;
+        const bool active = ch < d.channels;
+        const float gc = active ? to_f32(grad_out[item * d.channels + ch]) : 0.0f;
+        for (int j = 0; j < n; ++j) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int r = __shfl_sync(0xffffffffu, row[k], j);
+            const float w = __shfl_sync(0xffffffffu, wa[k], j);
+            if (!active || r < 0) continue;
+            const float contribution = w * gc;
+            const int64_t at = head0 + static_cast<int64_t>(r) * row_stride + ch;
+            if (fp.finite)
+              atomicAdd(acc + at, static_cast<unsigned long long>(
+                                      __double2ll_rn(static_cast<double>(contribution) * fp.scale)));
+            else
+              atomicAdd(grad_value + at, contribution);
+          }
         }
       }
     }
