@@ -526,8 +526,10 @@ def run_query_variant(args, cfg, dtype, rank, world, device):
         "vs_baseline": None,
         "dtype": _dtype_tag(dtype),
         "data": "synthetic",
-        "config": {"workload": _workload_name(sample, dtype, args), "parallelism": f"query-sharded x{world} + NCCL reduce_scatter(grad_value)"},
-        "gpu_launches": 2 * args.steps * world,
+        "config": {"workload": _workload_name(sample, dtype, args),
+                   "parallelism": f"query-sharded x{world} + per-image NCCL reduce_scatter(grad_value) overlapped "
+                                  "with the next image's backward"},
+        "gpu_launches": (2 if world == 1 else 1 + sample.batch) * args.steps * world,
         "clocks": clocks.summary(),
     }
 

@@ -20,7 +20,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from conftest import load_golden
-from muspace_b200.sharding import all_gather_grad_value, padded_numel, reduce_scatter_grad_value, shard_range
+from muspace_b200.sharding import (all_gather_grad_value, image_shard_numel, padded_numel, reduce_scatter_grad_value,
+                                   reduce_scatter_image, shard_range)
 
 
 def test_shard_range_covers_every_unit_once():
@@ -66,6 +67,10 @@ def _worker(rank, world, port, result_dir):
         gv, gl, gw = oracle_backward(*args, loc, w, grad)
         shard, offset = reduce_scatter_grad_value(torch.from_numpy(gv))
         full = all_gather_grad_value(shard, gv.shape)
+        # per camera image, as the overlapped GPU step exchanges it
+        image_shards = torch.empty(gv.shape[0], image_shard_numel(gv[0].size, world))
+        for i in range(gv.shape[0]):
+            reduce_scatter_image(torch.from_numpy(gv[i]), image_shards[i])
         # batch sharding: each rank owns whole batch entries, no exchange at all
         b0, b1 = shard_range(g["value"].shape[0], world, rank)
         bout = oracle_forward(g["value"][b0:b1], g["spatial_shapes"], g["level_start_index"],
@@ -73,6 +78,7 @@ def _worker(rank, world, port, result_dir):
         np.savez(
             os.path.join(result_dir, f"rank{rank}.npz"),
             out=out, gl=gl, gw=gw, shard=shard.numpy(), offset=offset, full=full.numpy(), bout=bout, q=(q0, q1), b=(b0, b1),
+            image_shards=image_shards.numpy(),
         )
     finally:
         dist.destroy_process_group()
@@ -97,3 +103,11 @@ def test_two_rank_query_and_batch_sharding_reproduce_the_single_process_answer(t
         assert not np.any(shard[valid:]), "padding must stay zero"
         np.testing.assert_allclose(r["full"], g["grad_value"], rtol=1e-5, atol=1e-5)
         np.testing.assert_allclose(r["bout"], g["output"][b0:b1], rtol=1e-5, atol=1e-5)
+        per_image = r["image_shards"]
+        for i in range(g["grad_value"].shape[0]):
+            flat = g["grad_value"][i].reshape(-1)
+            n = per_image.shape[1]
+            lo = rank * n
+            valid = max(0, min(n, flat.size - lo))
+            np.testing.assert_allclose(per_image[i, :valid], flat[lo : lo + valid], rtol=1e-5, atol=1e-5)
+            assert not np.any(per_image[i, valid:]), "padding must stay zero"
