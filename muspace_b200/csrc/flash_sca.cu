@@ -63,9 +63,8 @@ template <int G>
 struct Shape {
   static constexpr int kThreads = G >= 8 ? 256 : 32 * G;
   static constexpr int kGroups = kThreads / G;
-  static constexpr int kChunk = G < 4 ? G : 4;  // samples staged per chunk (forward) and per dot round
-  static constexpr int kStager = G / kChunk;
-  // backward: samples staged (and folded) per chunk, in rounds of kChunk
+  static constexpr int kChunk = G < 4 ? G : 4;  // samples per dot round of the backward
+  // samples staged per chunk (the backward folds them and takes its dots in rounds of kChunk)
   static constexpr int kBwdChunk = G < 8 ? kChunk : 8;
   static constexpr int kBwdStager = G / kBwdChunk;
   static constexpr int kSlots = kBwdChunk + 1;  // + padding against bank conflicts between groups
@@ -75,7 +74,7 @@ struct Shape {
 template <int G>
 struct GroupSmem {
   int pair[kMaxPairs];
-  float2 uv[kMaxPairs];
+  float2 uv[kMaxPairs];  // projection / image size
   int4 row[Shape<G>::kSlots];
   float4 wa[Shape<G>::kSlots];
   float4 geo[Shape<G>::kSlots];  // du, dv, attention weight, entry (int bits)
@@ -111,7 +110,8 @@ __device__ __forceinline__ int land_pairs(const Dims& d, const float* proj_b, co
     if (ok) {
       const int pos = n + __popc(rel & ((1u << sub) - 1u));
       s.pair[pos] = pr;
-      s.uv[pos] = make_float2(u, v);
+      // the projection normalised to the image, as each sample's base needs it
+      s.uv[pos] = make_float2(__fdiv_rn(u, img_w), __fdiv_rn(v, img_h));
     }
     lands |= static_cast<uint64_t>(rel) << k0;
     n += __popc(rel);
@@ -129,7 +129,7 @@ __device__ __forceinline__ int land_pairs(const Dims& d, const float* proj_b, co
 // entry) for the gradients.
 template <int G, bool kLevelMajor = false>
 __device__ __forceinline__ void stage(const Dims& d, const Map* maps, const float* off_item, const float* w_item,
-                                      float img_h, float img_w, int s, int samples, int slot, GroupSmem<G>& sm) {
+                                      int s, int samples, int slot, GroupSmem<G>& sm) {
   int4 r = make_int4(-1, -1, -1, -1);
   float4 wa = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -155,8 +155,8 @@ __device__ __forceinline__ void stage(const Dims& d, const Map* maps, const floa
     const int e = (level * d.points + point) * d.gz + iz;  // entry inside the (cell, head) block
     const float2 off = *reinterpret_cast<const float2*>(off_item + 2 * e);
     const float weight = w_item[e];
-    const float bu = __fsub_rn(__fmul_rn(__fdiv_rn(uv.x, img_w), static_cast<float>(m.w)), 0.5f);
-    const float bv = __fsub_rn(__fmul_rn(__fdiv_rn(uv.y, img_h), static_cast<float>(m.h)), 0.5f);
+    const float bu = __fsub_rn(__fmul_rn(uv.x, static_cast<float>(m.w)), 0.5f);
+    const float bv = __fsub_rn(__fmul_rn(uv.y, static_cast<float>(m.h)), 0.5f);
     const float su = __fadd_rn(bu, off.x), sv = __fadd_rn(bv, off.y);
     const float fu = floorf(su), fv = floorf(sv);
     // finite samples only (a non-finite offset samples nothing, as its corners fail every bound)
@@ -210,23 +210,31 @@ __device__ __forceinline__ float4 gather(const float* p, int row, int channels) 
 // values by a constant before sampling, so they receive no gradient.
 __device__ __forceinline__ float keep(float raw, float grad) { return fabsf(raw) <= 3.402823466e+38f ? grad : 0.0f; }
 
+// Samples the forward stages per round: 1 = one per lane round of the
+// backward (Shape::kBwdChunk: every lane of a group stages one), 0 = the dot
+// round size (Shape::kChunk: half the lanes stage).
+#ifndef FSCA_FWD_WIDE_CHUNK
+#define FSCA_FWD_WIDE_CHUNK 1
+#endif
+#define FSCA_FWD_CHUNK_OF(G) (FSCA_FWD_WIDE_CHUNK ? Shape<G>::kBwdChunk : Shape<G>::kChunk)
+
 // One item's sum over its samples: sum_k wa_k * value(row_k) for the lane's
-// slice, staging kChunk samples at a time. kSanitize reads a non-finite value
+// slice, staging FSCA_FWD_CHUNK_OF(G) samples at a time. kSanitize reads a non-finite value
 // as 0. All lanes of the warp call it with the warp's common trip count.
 template <int G, bool kSanitize>
 __device__ __forceinline__ float4 sum_item(const Dims& d, const Map* maps, const float* off_item, const float* w_item,
-                                           float img_h, float img_w, int trips, int samples, int sub,
-                                           const float* vb, GroupSmem<G>& sm) {
-  using Sh = Shape<G>;
+                                           int trips, int samples, int sub, const float* vb, GroupSmem<G>& sm) {
+  constexpr int Cs = FSCA_FWD_CHUNK_OF(G);
+  constexpr int kStager = G / Cs;
   float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  for (int s0 = 0; s0 < trips; s0 += Sh::kChunk) {
-    if (sub % Sh::kStager == 0) {
-      const int i = sub / Sh::kStager;
-      stage<G>(d, maps, off_item, w_item, img_h, img_w, s0 + i, samples, i, sm);
+  for (int s0 = 0; s0 < trips; s0 += Cs) {
+    if (sub % kStager == 0) {
+      const int i = sub / kStager;
+      stage<G>(d, maps, off_item, w_item, s0 + i, samples, i, sm);
     }
     __syncwarp();
 #pragma unroll
-    for (int i = 0; i < Sh::kChunk; ++i) {
+    for (int i = 0; i < Cs; ++i) {
       const int4 r4 = sm.row[i];
       const float4 w4 = sm.wa[i];
       const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
@@ -315,11 +323,11 @@ __global__ void FSCA_FWD_BOUNDS(G) forward_kernel(Dims d, Grid grid, float eps,
     // (the staging syncs need the whole warp) sums its item again with each
     // gathered value read as 0 when it is not finite, the reference's
     // _sanitize_value. Finite inputs never pay for the test per value.
-    float4 acc = sum_item<G, false>(d, maps, off_item, w_item, img_h, img_w, trips, samples, sub, vb, sm);
+    float4 acc = sum_item<G, false>(d, maps, off_item, w_item, trips, samples, sub, vb, sm);
     const bool finite = fabsf(acc.x) <= 3.402823466e+38f && fabsf(acc.y) <= 3.402823466e+38f &&
                         fabsf(acc.z) <= 3.402823466e+38f && fabsf(acc.w) <= 3.402823466e+38f;
     if (__any_sync(0xffffffffu, live && !finite))
-      acc = sum_item<G, true>(d, maps, off_item, w_item, img_h, img_w, trips, samples, sub, vb, sm);
+      acc = sum_item<G, true>(d, maps, off_item, w_item, trips, samples, sub, vb, sm);
     if (live) {
       const float inv = visible > 0 ? __fdiv_rn(1.0f, static_cast<float>(visible)) : 0.0f;
       *reinterpret_cast<float4*>(out + cell * d.channels + head * per_head + sub * 4) =
@@ -382,7 +390,7 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
     for (int s0 = 0; s0 < trips; s0 += Cs) {
       if (sub % Sh::kBwdStager == 0) {
         const int i = sub / Sh::kBwdStager;
-        stage<G, true>(d, maps, off_item, w_item, img_h, img_w, s0 + i, samples, i, sm);
+        stage<G, true>(d, maps, off_item, w_item, s0 + i, samples, i, sm);
       }
       __syncwarp();
       // samples of one level around the heights of a camera share corner rows
