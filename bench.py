@@ -57,6 +57,8 @@ def parse_args():
     p.add_argument("--dtype", choices=("bfloat16", "float32"), default=None)
     p.add_argument("--scaling", choices=("weak", "strong"), default="weak")
     p.add_argument("--variant", choices=("batch", "query"), default="batch")
+    p.add_argument("--per-image", action="store_true",
+                   help="--variant query: backward and grad_value reduce-scatter per camera image, overlapped")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--quiet", action="store_true", help="print only the JSON line")
@@ -489,7 +491,7 @@ def run_query_variant(args, cfg, dtype, rank, world, device):
 
     sample = cases.CONFIGS["c2"].with_(locations=cfg.locations)
     inp = cases.make_inputs(sample, dtype=dtype, seed=2333, device=device)
-    step = QueryShardedStep(inp, dtype, rank, world)
+    step = QueryShardedStep(inp, dtype, rank, world, per_image=args.per_image)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -527,9 +529,10 @@ def run_query_variant(args, cfg, dtype, rank, world, device):
         "dtype": _dtype_tag(dtype),
         "data": "synthetic",
         "config": {"workload": _workload_name(sample, dtype, args),
-                   "parallelism": f"query-sharded x{world} + per-image NCCL reduce_scatter(grad_value) overlapped "
-                                  "with the next image's backward"},
-        "gpu_launches": (2 if world == 1 else 1 + sample.batch) * args.steps * world,
+                   "parallelism": (f"query-sharded x{world} + per-image NCCL reduce_scatter(grad_value) overlapped "
+                                   "with the next image's backward") if args.per_image and world > 1 else
+                                  f"query-sharded x{world} + NCCL reduce_scatter(grad_value)"},
+        "gpu_launches": (1 + sample.batch if args.per_image and world > 1 else 2) * args.steps * world,
         "clocks": clocks.summary(),
     }
 
