@@ -15,10 +15,11 @@
 //
 // The sample geometry (level, unnormalised coordinate, the four corner rows
 // and bilinear weights) is the same for every lane of a group, so it is not
-// computed G times: the samples are taken in chunks of C = min(G, 8), the
-// lane at sub = i * G / C computes sample i of the chunk and stages its four
-// corner rows and w_k * a in shared memory, and the whole group then reads
-// them back (one broadcast load each) while it gathers. Items are ordered
+// computed G times: the samples are taken in chunks of 8 (4 for head-rows of
+// at most 4 samples; at most 4 G), lane sub computes samples sub, sub + G, ...
+// of the chunk and stages their four corner rows and w_k * a in shared
+// memory, and the whole group then reads them back (one broadcast load each)
+// while it gathers. Items are ordered
 // batch-major, so at any moment the CTAs in flight gather from one or two
 // cameras' value maps, which stay resident in L2. Any other D takes the
 // scalar kernel below.
