@@ -57,6 +57,13 @@ struct FwdSlots {  // 1-lane groups (256 per CTA) stage 4 samples so the slots f
 
 // Lane bytes of the forward for bf16 / fp32 storage (16: one 16-byte load per
 // corner; 32: two, half the lanes per head-row).
+// 1: corners outside their level are gathered from an in-level row of the same
+// sample with weight 0 instead of being skipped (no compare and zero-fill per
+// corner); a head-row whose sum comes out non-finite (which a non-finite
+// value read that way could cause) is summed again the exact way.
+#ifndef MSDA_FWD_SUBST
+#define MSDA_FWD_SUBST 1
+#endif
 #ifndef MSDA_FWD_LANE_BYTES_BF16
 #define MSDA_FWD_LANE_BYTES_BF16 16
 #endif
@@ -69,7 +76,32 @@ struct FwdSlots {  // 1-lane groups (256 per CTA) stage 4 samples so the slots f
 // the head's value map; lp / wp at the head-row's locations / weights; row /
 // wa at the group's staging slots. Every lane of the warp must call it (it
 // syncs the warp), live = false for a lane group without an item.
-template <typename T, int G, int kBytes, int kChunk = MSDA_FWD_CHUNK>
+// The staged corners of a sample for the substituting gather: every corner
+// outside its level takes the row of an in-level corner of the same sample
+// (row 0 of the map when it has none, which the caller guarantees exists) and
+// weight 0, so every corner can be loaded unconditionally.
+__device__ __forceinline__ void substitute_outside_corners(int4* row, float4* wa) {
+  int4 r = *row;
+  float4 w = *wa;
+  const int any = r.x >= 0 ? r.x : r.y >= 0 ? r.y : r.z >= 0 ? r.z : r.w >= 0 ? r.w : 0;
+  if (r.x < 0) r.x = any, w.x = 0.0f;
+  if (r.y < 0) r.y = any, w.y = 0.0f;
+  if (r.z < 0) r.z = any, w.z = 0.0f;
+  if (r.w < 0) r.w = any, w.w = 0.0f;
+  *row = r;
+  *wa = w;
+}
+
+// Whether every channel pair of acc is finite.
+template <int kPairs>
+__device__ __forceinline__ bool finite_pairs(const float2 (&acc)[kPairs]) {
+  bool ok = true;
+#pragma unroll
+  for (int q = 0; q < kPairs; ++q) ok = ok && fabsf(acc[q].x) <= 3.402823466e+38f && fabsf(acc[q].y) <= 3.402823466e+38f;
+  return ok;
+}
+
+template <typename T, int G, int kBytes, int kChunk = MSDA_FWD_CHUNK, bool kSubst = false>
 __device__ __forceinline__ void gather_head_row(const Level* levels, int points, int samples, bool live,
                                                 const T* vbase, int row_stride, const T* lp, const T* wp, int sub,
                                                 int4* row, float4* wa, float2 (&acc)[Slice<T, kBytes>::kPairs]) {
@@ -80,7 +112,10 @@ __device__ __forceinline__ void gather_head_row(const Level* levels, int points,
   for (int i = 0; i < kPairs; ++i) acc[i] = make_float2(0.0f, 0.0f);
   for (int s0 = 0; s0 < samples; s0 += C) {
 #pragma unroll
-    for (int i = sub; i < C; i += G) stage_sample(levels, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
+    for (int i = sub; i < C; i += G) {
+      stage_sample(levels, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
+      if constexpr (kSubst) substitute_outside_corners(row + i, wa + i);
+    }
     __syncwarp();
 #pragma unroll kFwdUnroll
     for (int i = 0; i < C; ++i) {
@@ -90,9 +125,13 @@ __device__ __forceinline__ void gather_head_row(const Level* levels, int points,
       const float was[4] = {w4.x, w4.y, w4.z, w4.w};
       Words<kWords> raw[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        raw[k] = rows[k] >= 0 ? ldg_words<kBytes>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
-                              : zero_words<kWords>();
+      for (int k = 0; k < 4; ++k) {
+        if constexpr (kSubst)
+          raw[k] = ldg_words<kBytes>(vbase + static_cast<int64_t>(rows[k]) * row_stride);
+        else
+          raw[k] = rows[k] >= 0 ? ldg_words<kBytes>(vbase + static_cast<int64_t>(rows[k]) * row_stride)
+                                : zero_words<kWords>();
+      }
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
 #if MSDA_FWD_PACKED
@@ -156,8 +195,20 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_FWD_MINBLOCKS) forward_vec_k
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
     const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     float2 acc[kPairs];
-    gather_head_row<T, G, kBytes, kChunk>(levels, d.points, samples, live, vbase, row_stride, loc + item * samples * 2,
-                                  weight + item * samples, sub, s_row + base, s_wa + base, acc);
+    const T* lp = loc + item * samples * 2;
+    const T* wp = weight + item * samples;
+    // substituting needs a row 0 to fall back on (an empty value map has none);
+    // it measured faster for bf16 only (c4 forward 2.49 -> 2.40 ms; c1 fp32
+    // 0.190 -> 0.198 ms)
+    bool exact = !(MSDA_FWD_SUBST && sizeof(T) == 2) || d.spatial_size == 0;
+    if (!exact) {
+      gather_head_row<T, G, kBytes, kChunk, true>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub,
+                                                  s_row + base, s_wa + base, acc);
+      exact = __any_sync(0xffffffffu, live && !finite_pairs(acc));  // warp-uniform, rare
+    }
+    if (exact)
+      gather_head_row<T, G, kBytes, kChunk>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub,
+                                            s_row + base, s_wa + base, acc);
     if (live) store_slice<T, kBytes>(out + item * d.channels + sub * kCh, acc);
   }
 }
@@ -202,8 +253,18 @@ __global__ void __launch_bounds__(kCtaThreads) scatter_div_vec_kernel(
     const int64_t lrow = (image * d.queries + q) * d.heads + h;  // rebatched (image, q, h) row
     const T* vbase = value + (image * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     float2 acc[kPairs];
-    gather_head_row<T, G, 16>(levels, d.points, samples, live, vbase, row_stride, loc + lrow * samples * 2,
-                          weight + lrow * samples, sub, s_row + base, s_wa + base, acc);
+    const T* lp = loc + lrow * samples * 2;
+    const T* wp = weight + lrow * samples;
+    // substituted out-of-level corners as in forward_vec_kernel (bf16 only)
+    bool exact = !(MSDA_FWD_SUBST && sizeof(T) == 2) || d.spatial_size == 0;
+    if (!exact) {
+      gather_head_row<T, G, 16, MSDA_FWD_CHUNK, true>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub,
+                                                      s_row + base, s_wa + base, acc);
+      exact = __any_sync(0xffffffffu, live && !finite_pairs(acc));
+    }
+    if (exact)
+      gather_head_row<T, G, 16>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub, s_row + base,
+                                s_wa + base, acc);
     const int64_t bev = index[q];
     if (live && bev >= 0 && bev < sd.num_query) {
       const int64_t srow = b * sd.num_query + bev;

@@ -346,3 +346,32 @@ def test_c4_batch_slices_equal_the_whole_and_grad_value_is_additive(cuda_device)
         total += pgv
     torch.testing.assert_close(total, gv, rtol=1e-4, atol=1e-4)
     _subset_check(inp, out, (gv, gl, gw), BF16_TOL, rows=24, seed=1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_non_finite_values_next_to_out_of_level_corners(cuda_device, dtype):
+    """Infinite and NaN values at pixel 0 and along a border, with samples
+    half outside their level: the forward (whose bf16 kernels gather an
+    out-of-level corner from an in-level row with weight 0, and sum a head-row
+    again the exact way when its sum is not finite) matches the oracle
+    element for element, non-finite elements included."""
+    g = _random_case(32, 3, 3, seed=77, queries=40, heads=2)
+    value = g["value"].copy()
+    value[:, 0] = np.inf            # row 0 of level 0 (the fall-back row of fully outside samples)
+    value[0, 6, 1] = np.nan         # on level 0's top border (5 x 7 map)
+    value[1, 35, 0] = -np.inf       # level 1's first pixel
+    g["value"] = value
+    q = {k: (torch.from_numpy(v).to(dtype).float().numpy() if v.dtype == np.float32 else v) for k, v in g.items()}
+    exp = oracle_forward(*[q[k] for k in INPUTS])
+    inp = {k: torch.from_numpy(v).to(cuda_device) for k, v in q.items()}
+    inp = {k: (v.to(dtype) if v.dtype.is_floating_point else v) for k, v in inp.items()}
+    out = torch.empty(inp["grad_output"].shape, dtype=dtype, device=cuda_device)
+    native.native_function("ms_deform_attn_forward")(*[inp[k] for k in INPUTS], out, 64)
+    got = out.float().cpu()
+    expected = torch.from_numpy(np.asarray(exp, dtype=np.float32))
+    assert not torch.isfinite(expected).all()
+    assert torch.equal(torch.isnan(got), torch.isnan(expected))
+    assert torch.equal(torch.isinf(got), torch.isinf(expected))
+    tol = FP32_TOL if dtype == torch.float32 else BF16_TOL
+    fin = torch.isfinite(expected)
+    torch.testing.assert_close(got[fin], expected[fin], rtol=tol, atol=tol)
