@@ -90,6 +90,22 @@ def _peaks() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
 
 
+# Payload rate of red.global.add.v4.f32 into an L2-resident region with 128 B
+# per 8-lane group (whole lines), measured on this pool's B200s (6.34-6.39
+# TB/s over 296-1184 CTAs); bulk reductions from shared memory reached less.
+RED_PEAK_GBS = 6390.0
+RED_PEAK_SOURCE = "measured: red.global.add.v4.f32, 128-byte lines into an L2-resident region (B200)"
+
+
+def _red_bytes(kernel: str, launch_units: float):
+    """RED payload bytes per launch from the committed ncu summary, scaled by units."""
+    try:
+        entry = json.loads((ROOT / "profiles" / "dram_traffic.json").read_text())[kernel]
+        return entry["red_bytes"] / entry["units"] * launch_units
+    except Exception:
+        return None
+
+
 def _traffic(kernel: str, workload: str, launch_units: float):
     """DRAM bytes per launch from the committed ncu summary, scaled by units."""
     path = ROOT / "profiles" / "dram_traffic.json"
@@ -390,6 +406,15 @@ def run_b200(args, cfg, dtype, rank, world, device):
         "clocks": clocks.summary(),
         "e2e": e2e,
     }
+    red = _red_bytes("ms_deformable_backward", local.batch)
+    if red is not None:
+        # the limit that binds the backward: its grad_value RED payload (ncu)
+        # against the rate L2 reductions reach at best
+        red_gbs = red / (bwd_ms / 1e3) / 1e9
+        line["reduction_roofline"] = {
+            "bound": "L2 reductions", "kernel": "ms_deformable_backward", "achieved": round(red_gbs, 1),
+            "peak": RED_PEAK_GBS, "unit": "GB/s", "frac": round(red_gbs / RED_PEAK_GBS, 4),
+            "payload_bytes": int(red), "peak_source": RED_PEAK_SOURCE}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, dtype)
     return line
