@@ -439,7 +439,10 @@ def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device) -> floa
     import torch.distributed as dist
 
     s_in, s_comp, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
-    host_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in slot.outputs] for slot in slots]
+    # one pinned output set: the D2H copies of the slots run one after another
+    # on s_out, so they never write it at the same time (and a rank pins its
+    # inputs and outputs once, not twice, which matters with 8 ranks a node)
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in slots[0].outputs]
     in_done = [torch.cuda.Event() for _ in slots]
     comp_done = [torch.cuda.Event() for _ in slots]
     out_done = [torch.cuda.Event() for _ in slots]
@@ -459,7 +462,7 @@ def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device) -> floa
         comp_done[j].record(s_comp)
         s_out.wait_event(comp_done[j])
         with torch.cuda.stream(s_out):
-            for dst, src in zip(host_out[j], slot.outputs):
+            for dst, src in zip(host_out, slot.outputs):
                 dst.copy_(src, non_blocking=True)
         out_done[j].record(s_out)
 
