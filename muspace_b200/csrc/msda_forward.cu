@@ -71,11 +71,6 @@ struct FwdSlots {  // 1-lane groups (256 per CTA) stage 4 samples so the slots f
 #define MSDA_FWD_LANE_BYTES_F32 16
 #endif
 
-// acc (this lane's channel pairs) += sum over the head-row's samples of
-// sum_k (w_k a) v_k. vbase points at the lane's channel slice of pixel 0 of
-// the head's value map; lp / wp at the head-row's locations / weights; row /
-// wa at the group's staging slots. Every lane of the warp must call it (it
-// syncs the warp), live = false for a lane group without an item.
 // The staged corners of a sample for the substituting gather: every corner
 // outside its level takes the row of an in-level corner of the same sample
 // (row 0 of the map when it has none, which the caller guarantees exists) and
@@ -101,6 +96,13 @@ __device__ __forceinline__ bool finite_pairs(const float2 (&acc)[kPairs]) {
   return ok;
 }
 
+// acc (this lane's channel pairs) += sum over the head-row's samples of
+// sum_k (w_k a) v_k. vbase points at the lane's channel slice of pixel 0 of
+// the head's value map; lp / wp at the head-row's locations / weights; row /
+// wa at the group's staging slots. Every lane of the warp must call it (it
+// syncs the warp), live = false for a lane group without an item.
+// kSubst: the staged corners outside their level are substituted
+// (substitute_outside_corners) and every corner is loaded.
 template <typename T, int G, int kBytes, int kChunk = MSDA_FWD_CHUNK, bool kSubst = false>
 __device__ __forceinline__ void gather_head_row(const Level* levels, int points, int samples, bool live,
                                                 const T* vbase, int row_stride, const T* lp, const T* wp, int sub,
