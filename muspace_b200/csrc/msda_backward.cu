@@ -63,6 +63,10 @@ namespace msda {
 #ifndef MSDA_BWD_DEDUP
 #define MSDA_BWD_DEDUP 1
 #endif
+// 1: the lane-pair kernel also takes bf16 head-rows of at most 4 samples.
+#ifndef MSDA_PAIR_SHORT
+#define MSDA_PAIR_SHORT 1
+#endif
 // Samples per dot round (their partial dots live in registers: 4 per sample)
 // and CTAs per SM the register budget is sized for; measured on B200 (fp32
 // D = 32: rounds of 2 at 3 CTAs/SM beat rounds of 4 at 2 or 3; 4 CTAs/SM at
@@ -501,12 +505,12 @@ template <typename T>
 static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t stream) {
 #if MSDA_BWD_PAIR
   // The lane-pair kernel where it measured faster on B200: bf16 rows of 2 or 4
-  // chunks of 16 bytes (D = 16, 32) with more than 4 samples per head-row
-  // (c2 / c4: backward 1.18 -> 1.11 ms / 9.38 -> 8.81 ms). fp32 rows (4
-  // chunks per lane, one corner in flight) and single-level rows ran slower
-  // than backward_vec_kernel.
+  // chunks of 16 bytes (D = 16, 32) (c2 / c4: backward 1.18 -> 1.11 ms /
+  // 9.38 -> 8.81 ms; at 4 CTAs/SM also single-level rows of 4 samples: c3
+  // 0.287 -> 0.277 ms, bevformer-1l bf16 0.331 -> 0.325 ms). fp32 rows (4
+  // chunks per lane, one corner in flight) ran slower than backward_vec_kernel.
   if constexpr (sizeof(T) == 2) {
-    if (d.levels * d.points > 4 && vec_lanes(d.channels, sizeof(T), 16, a) != 0 &&
+    if ((MSDA_PAIR_SHORT || d.levels * d.points > 4) && vec_lanes(d.channels, sizeof(T), 16, a) != 0 &&
         vec_lanes(d.channels, 4, 16, a) != 0) {
       switch (d.channels * static_cast<int>(sizeof(T)) / 32) {
         case 1: return launch_backward_pair<T, 1>(d, a, stream);
