@@ -36,8 +36,8 @@
 //       grad_w = sum_k w_k T_k,
 //       grad_x = W a (hh (T_1 - T_0) + lh (T_3 - T_2)),
 //       grad_y = H a (hw (T_2 - T_0) + lw (T_3 - T_1)).
-// That is backward_vec_kernel. For bf16 D = 16 / 32 with more than 4 samples
-// per head-row (every BEVFormer shape) backward_pair_kernel runs instead: the
+// That is backward_vec_kernel. For bf16 D = 16 / 32 (every BEVFormer shape)
+// backward_pair_kernel runs instead: the
 // same stage and fold, then a lane pair forms one sample's dots (no transpose
 // reduction) and every lane sends 4-channel fp32 REDs (description above the
 // kernel).
