@@ -14,11 +14,17 @@ needed between steps.
 
 ``value`` is effective GB/s: the algorithmic (compulsory) bytes of the step
 (fwd: value + locations + weights + output; bwd: the same reads plus fp32
-writes of the three gradients) over the device time, summed over ranks. Each
-rank processes its own 48-image shard (weak scaling, no collective on the data
-path); ``--scaling strong`` splits the 48 images across ranks instead.
-``--variant query`` runs the bs=1 form: one 6-camera sample, queries split
-across ranks, value replicated, fp32 ``grad_value`` reduce-scattered with NCCL.
+writes of the three gradients) over the device time, whole job. With N GPUs the
+48 images of config 4 are split across the ranks, 48 / N each (strong scaling,
+config 4 as stated: one batch sharded by batch x camera, no collective on the
+data path), and the time is the slowest rank's; ``--scaling weak`` gives every
+rank its own 48-image shard instead. ``--variant query`` runs the bs=1 form: one
+6-camera sample, queries split across ranks, value replicated, fp32
+``grad_value`` reduce-scattered with NCCL; its ``kernels_ms`` separate the
+kernels from the reduce-scatter. ``--protocol reference`` times the reference's
+published-case protocol instead (20 warm-ups, 5 repeats x 100 launches, median;
+``benchmarks/_harness.py:226-260``) for both the reference's timed closure and
+this build's step, next to the published figures.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -53,15 +59,19 @@ def parse_args():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--config", default="c4", choices=sorted(cases.CONFIGS))
+    p.add_argument("--config", default=None, choices=sorted(cases.CONFIGS),
+                   help="default: c4 (bevformer-1l with --protocol reference)")
     p.add_argument("--dtype", choices=("bfloat16", "float32"), default=None)
-    p.add_argument("--scaling", choices=("weak", "strong"), default="weak")
+    p.add_argument("--scaling", choices=("weak", "strong"), default="strong",
+                   help="strong (default): the workload's images split across the ranks; weak: a whole workload per rank")
     p.add_argument("--variant", choices=("batch", "query"), default="batch")
     p.add_argument("--per-image", action="store_true",
                    help="--variant query: backward and grad_value reduce-scatter per camera image, overlapped")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--quiet", action="store_true", help="print only the JSON line")
+    p.add_argument("--protocol", choices=("contract", "reference"), default="contract",
+                   help="reference: the reference's published-case timing protocol (p50 of 5 x 100 launches)")
     p.add_argument("--op", choices=("msda", "deformable_aggregation", "flash_sca", "sca_scatter"), default="msda",
                    help="msda (default: the headline workload) or one of the ops built next to it")
     return p.parse_args()
@@ -257,9 +267,10 @@ def run_reference(args, cfg, dtype, rank: int):
 def _workload_name(cfg, dtype, args) -> str:
     if args.variant == "query":
         return f"config 4 bs=1 variant: {cfg.name} shapes at batch 6, queries split across ranks, grad_value reduce-scatter"
+    label = "config 4: BEVFormer-base SCA MSDA fwd+bwd" if cfg.name == "c4" else f"{cfg.name}: {cfg.description}"
     return (
-        f"config 4: BEVFormer-base SCA MSDA fwd+bwd, {cfg.batch} camera images per "
-        f"{'rank' if args.scaling == 'weak' else 'job'}, {_dtype_tag(dtype)} storage, fp32 accumulate"
+        f"{label}, {cfg.batch} images per {'rank' if args.scaling == 'weak' else 'job'}, "
+        f"{_dtype_tag(dtype)} storage, fp32 accumulate"
     )
 
 
@@ -307,11 +318,16 @@ def run_b200(args, cfg, dtype, rank, world, device):
     if args.variant == "query":
         return run_query_variant(args, cfg, dtype, rank, world, device)
     if args.scaling == "strong":
-        if cfg.batch % world:
-            raise SystemExit(f"strong scaling needs batch {cfg.batch} divisible by {world}")
-        local = cfg.with_(batch=cfg.batch // world)
+        from muspace_b200.sharding import shard_range
+
+        b0, b1 = shard_range(cfg.batch, world, rank)
+        if b1 == b0:
+            raise SystemExit(f"strong scaling: {world} ranks for {cfg.batch} images leaves rank {rank} without work")
+        local = cfg.with_(batch=b1 - b0)
+        job_total = cases.compulsory_bytes(cfg, dtype)["total"]
     else:
         local = cfg
+        job_total = cases.compulsory_bytes(cfg, dtype)["total"] * world
     inp = cases.make_inputs(local, dtype=dtype, seed=2333 + 7919 * rank, device=device)
     step = Step(inp, dtype, device)
     units = cases.compulsory_bytes(local, dtype)
@@ -348,10 +364,9 @@ def run_b200(args, cfg, dtype, rank, world, device):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    job_bytes = (fwd_bytes + bwd_bytes) * world
-    value = job_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
+    value = job_total * args.steps / (elapsed_ms / 1e3) / 1e9
 
-    e2e = None if args.no_e2e else run_e2e(args, local, dtype, inp, device, world, distributed)
+    e2e = None if args.no_e2e else run_e2e(args, local, dtype, inp, device, job_total, distributed)
 
     if rank != 0:
         return None
@@ -375,15 +390,16 @@ def run_b200(args, cfg, dtype, rank, world, device):
         "dtype": _dtype_tag(dtype),
         "data": "synthetic",
         "config": {
-            "workload": _workload_name(local, dtype, args),
+            "workload": _workload_name(cfg, dtype, args),
             "batch_per_rank": local.batch,
-            "global_batch": local.batch * world,
+            "global_batch": cfg.batch if args.scaling == "strong" else cfg.batch * world,
             "queries": local.queries,
             "levels": [list(s) for s in local.shapes],
             "points": local.points,
             "heads": local.heads,
             "channels": local.channels,
-            "parallelism": f"batch-sharded x{world} (no collective)",
+            "parallelism": (f"batch x camera sharded over {world} ranks (no collective)" if world > 1
+                            else "one GPU"),
             "l2": f"inputs {sum(t.numel() * t.element_size() for t in inp.values()) / 1e9:.2f} GB per rank > 126 MB L2; no flush",
             "scope": "forward launch + grad_value zero fill + backward launch through the C-ABI (reference forward-backward scope)",
             "compulsory_bytes_per_step_per_rank": fwd_bytes + bwd_bytes,
@@ -490,7 +506,7 @@ E2E_PATH = ("pinned host buffers -> cudaMemcpyAsync H2D -> {calls} (C-ABI) -> cu
             "two device buffer sets, H2D / compute / D2H on three streams")
 
 
-def run_e2e(args, local, dtype, inp, device, world, distributed):
+def run_e2e(args, local, dtype, inp, device, job_total, distributed):
     """The same step through the C-ABI with host buffers: pinned H2D of the
     inputs and D2H of the output and the three gradients, every step."""
     keys = [k for k in inp if k not in ("spatial_shapes", "level_start_index")]
@@ -502,9 +518,8 @@ def run_e2e(args, local, dtype, inp, device, world, distributed):
         slots.append(E2ESlot([dev_in[k] for k in keys], [step.out, step.gv, step.gl, step.gw], step))
     steps = max(3, min(args.steps, 10))
     ms = pipelined_e2e(slots, host_in, steps, distributed, device)
-    nbytes = cases.compulsory_bytes(local, dtype)["total"] * world
     return {
-        "value": round(nbytes / (ms / 1e3) / 1e9, 3),
+        "value": round(job_total / (ms / 1e3) / 1e9, 3),
         "unit": "GB/s",
         "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
         "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in slots[0].outputs),
@@ -540,6 +555,20 @@ def run_query_variant(args, cfg, dtype, rank, world, device):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item()) / args.steps
     nbytes = cases.compulsory_bytes(sample, dtype)["total"]
+    # per-phase device time (whole-batch exchange): events between the
+    # launches on the current stream, a separate pass after the timed one
+    kernels_ms = None
+    if not args.per_image:
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+        for e in ev:
+            step(e)
+        torch.cuda.synchronize()
+        phases = torch.tensor([statistics.mean(e[i].elapsed_time(e[i + 1]) for e in ev) for i in range(4)],
+                              dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(phases, op=dist.ReduceOp.MAX)
+        kernels_ms = {k: round(float(v), 4) for k, v in
+                      zip(("forward", "grad_value_fill", "backward", "reduce_scatter"), phases.tolist())}
     if rank != 0:
         return None
     return {
@@ -560,6 +589,7 @@ def run_query_variant(args, cfg, dtype, rank, world, device):
                    "parallelism": (f"query-sharded x{world} + per-image NCCL reduce_scatter(grad_value) overlapped "
                                    "with the next image's backward") if args.per_image and world > 1 else
                                   f"query-sharded x{world} + NCCL reduce_scatter(grad_value)"},
+        "kernels_ms": kernels_ms,
         "gpu_launches": (1 + sample.batch if args.per_image and world > 1 else 2) * args.steps * world,
         "clocks": clocks.summary(),
     }
@@ -803,8 +833,105 @@ def run_op(args, rank, world, device):
     return line
 
 
+# The reference's only published numbers for this path: the
+# bevformer-1l case, forward-backward scope, p50 of 5 repeats x 100 launches
+# after 20 warm-ups (benchmarks/msda/README.md:72-73 in the muSPACE tree).
+PUBLISHED = {
+    ("bevformer-1l", torch.float32): {
+        "S5000_p50_ms": 4.2387, "S5000_normalised_to_A100_bandwidth_ms": 3.5049, "mmcv_A100_p50_ms": 4.0895,
+        "source": "benchmarks/msda/README.md:72 (MTT S5000; mmcv CUDA MSDA on A100 80GB PCIe)"},
+    ("bevformer-1l", torch.bfloat16): {
+        "S5000_p50_ms": 3.9933, "source": "benchmarks/msda/README.md:73 (MTT S5000; no mmcv bf16 path to time)"},
+}
+
+
+def protocol_measure(launch, warmup=20, iterations=100, repeats=5):
+    """The reference harness's timing (benchmarks/_harness.py:226-260): warm-up
+    launches, then `repeats` samples, each the mean of `iterations` launches
+    between two device events; the published figure is the median sample."""
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize()
+    samples = []
+    for _ in range(repeats):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iterations):
+            launch()
+        end.record()
+        end.synchronize()
+        samples.append(start.elapsed_time(end) / iterations)
+    return samples
+
+
+def run_protocol(args, cfg, dtype, device):
+    """--protocol reference: the published case timed the reference's way,
+    through the same C-ABI entry points its harness calls, in two scopes:
+    the reference's timed closure (benchmarks/msda/benchmark_msda.py:98-119:
+    output allocation, forward launch, three zero-filled accumulators,
+    grad_output.contiguous(), backward launch) and this build's step (forward,
+    zero fill of grad_value only -- grad_loc / grad_w are written everywhere
+    -- backward)."""
+    from muspace_b200.runtime.native import native_function
+
+    fwd, bwd = native_function("ms_deform_attn_forward"), native_function("ms_deform_attn_backward")
+    # drawn on the CPU from the reference's seeds (2333 forward, 2334 backward), then moved
+    inp = {k: v.to(device) for k, v in cases.make_inputs(cfg, dtype=dtype, seed=2333, device="cpu").items()}
+    grad = inp["grad_output"]
+    names = ("value", "spatial_shapes", "level_start_index", "sampling_locations", "attention_weights")
+    a = [inp[n] for n in names]
+    value, loc, weight = a[0], a[3], a[4]
+
+    def reference_closure():
+        output = value.new_empty((value.size(0), loc.size(1), value.size(2) * value.size(3)))
+        fwd(*a, output, 64)
+        gv = torch.zeros(value.shape, dtype=torch.float32, device=device)
+        gl = torch.zeros(loc.shape, dtype=torch.float32, device=device)
+        gw = torch.zeros(weight.shape, dtype=torch.float32, device=device)
+        bwd(*a, grad.contiguous(), gv, gl, gw, 64)
+
+    step = Step(inp, dtype, device)
+    with Clocks(device.index) as clocks:
+        ref_samples = protocol_measure(reference_closure)
+        own_samples = protocol_measure(step)
+    ref_p50, own_p50 = statistics.median(ref_samples), statistics.median(own_samples)
+    nbytes = cases.compulsory_bytes(cfg, dtype)["total"]
+    peak, peak_src = _peaks()
+    published = PUBLISHED.get((cfg.name, dtype))
+    line = {
+        "metric": "MSDA fwd+bwd p50 ms, reference published-case protocol",
+        "value": round(ref_p50, 4),
+        "unit": "ms",
+        "n_gpus": 1,
+        "higher_is_better": False,
+        "dtype": _dtype_tag(dtype),
+        "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: {cfg.description}", "protocol":
+                   "20 warm-up launches, 5 repeats x 100 launches between device events, median repeat "
+                   "(benchmarks/_harness.py:226-260)",
+                   "scope": "the reference's timed closure: output allocation, forward, three torch.zeros "
+                            "accumulators, grad_output.contiguous(), backward (benchmarks/msda/benchmark_msda.py:98-119)",
+                   "compulsory_bytes": nbytes},
+        "reference_closure": {"p50_ms": round(ref_p50, 4), "samples_ms": [round(x, 4) for x in ref_samples],
+                              "effective_gbs": round(nbytes / (ref_p50 / 1e3) / 1e9, 1),
+                              "roofline_frac": round(nbytes / (ref_p50 / 1e3) / 1e9 / peak, 4)},
+        "own_step": {"p50_ms": round(own_p50, 4), "samples_ms": [round(x, 4) for x in own_samples],
+                     "effective_gbs": round(nbytes / (own_p50 / 1e3) / 1e9, 1),
+                     "roofline_frac": round(nbytes / (own_p50 / 1e3) / 1e9 / peak, 4),
+                     "scope": "forward, grad_value zero fill, backward (grad_loc / grad_w written, not zeroed)"},
+        "peak": {"hbm_gbs": peak, "source": peak_src},
+        "published": published,
+        "clocks": clocks.summary(),
+    }
+    if published:
+        line["speedup_vs_published"] = {k: round(v / ref_p50, 2) for k, v in published.items() if k.endswith("_ms")}
+    return line
+
+
 def main():
     args = parse_args()
+    if args.config is None:
+        args.config = "bevformer-1l" if args.protocol == "reference" else "c4"
     cfg = cases.CONFIGS[args.config]
     dtype = _dtype(args, cfg)
     rank = int(os.environ.get("RANK", "0"))
@@ -823,6 +950,11 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    if args.protocol == "reference":
+        if world != 1 or args.op != "msda":
+            raise SystemExit("--protocol reference times the MSDA published case on one GPU")
+        print(json.dumps(run_protocol(args, cfg, dtype, device)), flush=True)
+        return
     try:
         line = run_op(args, rank, world, device) if args.op != "msda" else run_b200(args, cfg, dtype, rank, world, device)
     finally:

@@ -424,6 +424,22 @@ int msda_backward_static_scratch(msda_dtype_t dtype, const msda_dims_t* dims, co
             "problem needs " + std::to_string(need) + " bytes of scratch, the static scratch holds " +
                 std::to_string(msda::static_scratch_capacity()) +
                 " (about 1M head-rows B * Lq * Hh); use msda_backward for larger calls");
+    if (!empty) {
+      // The scratch address is the current device's; the stream and the data
+      // must belong to that device, or the kernels would get another GPU's
+      // array.
+      int current = -1, stream_device = -1;
+      check_launch(cudaGetDevice(&current), "cudaGetDevice");
+      check_launch(cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_device), "cudaStreamGetDevice");
+      require(stream_device == current, "stream is on CUDA device " + std::to_string(stream_device) +
+                                            ", the current device is " + std::to_string(current));
+      cudaPointerAttributes attr{};
+      check_launch(cudaPointerGetAttributes(&attr, value), "cudaPointerGetAttributes");
+      require(attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged,
+              "value is not device memory");
+      require(attr.device == current, "value is on CUDA device " + std::to_string(attr.device) +
+                                          ", the current device is " + std::to_string(current));
+    }
     void* scratch = nullptr;
     if (need > 0) check_launch(msda::static_scratch_address(&scratch), "static scratch set-up");
     check_launch(msda::launch_backward_on_scratch(dt, kd, a, scratch, static_cast<cudaStream_t>(stream)),

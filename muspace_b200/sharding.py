@@ -133,15 +133,26 @@ class QueryShardedStep:
         self.comm = torch.cuda.Stream(device) if self.per_image else None
         self.computed = [torch.cuda.Event() for _ in range(images)] if self.per_image else []
 
-    def __call__(self) -> torch.Tensor:
+    def __call__(self, events=None) -> torch.Tensor:
+        """One step. ``events`` (optional, whole-batch exchange only): five
+        CUDA events recorded on the current stream before the forward, after
+        the forward, after the zero fill, after the backward and after the
+        reduce-scatter, so a caller can split kernel time from exchange time."""
         args = (self.value, self.shapes, self.start, self.loc, self.weight)
+        mark = (lambda i: events[i].record()) if events is not None and not self.per_image else (lambda i: None)
+        mark(0)
         self.fwd(*args, self.out, 64)
+        mark(1)
         self.gv.zero_()
+        mark(2)
         if not self.per_image:
             self.bwd(*args, self.grad_out, self.gv, self.gl, self.gw, 64)
+            mark(3)
             if self.world == 1:
+                mark(4)
                 return self.gv.view(-1)
             shard, _ = reduce_scatter_grad_value(self.gv)
+            mark(4)
             return shard
         compute = torch.cuda.current_stream(self.gv.device)
         for i in range(self.value.shape[0]):

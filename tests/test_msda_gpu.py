@@ -322,6 +322,57 @@ def test_baseline_sizes_match_oracle_on_sampled_rows(cuda_device, config, dtype)
     assert torch.equal(out, out2)
 
 
+def _image_check(inp, out, grads, b, dtype_tol, what):
+    """Every element of image b -- output, grad_value, grad_loc, grad_w --
+    against the C oracle run on that image alone (an image's head-rows only
+    read its own value map and only write its own grad_value)."""
+    img = {k: (v if k in ("spatial_shapes", "level_start_index") else v[b : b + 1]) for k, v in inp.items()}
+    args = [img[k].float().cpu().numpy() if img[k].dtype.is_floating_point else img[k].cpu().numpy() for k in INPUTS]
+    exp_out = oracle_forward(*args)
+    exp_gv, exp_gl, exp_gw = oracle_backward(*args, img["grad_output"].float().cpu().numpy())
+    gv, gl, gw = (g[b : b + 1] for g in grads)
+    _close(out[b : b + 1], exp_out, dtype_tol, f"{what} image {b} output")
+    # fp32 gradient buffers from identical (quantised) inputs: fp32 tolerance
+    _close(gv, exp_gv, FP32_TOL, f"{what} image {b} grad_value")
+    _close(gl, exp_gl, FP32_TOL, f"{what} image {b} grad_loc")
+    _close(gw, exp_gw, FP32_TOL, f"{what} image {b} grad_w")
+
+
+@pytest.mark.parametrize(
+    "config,dtype,images",
+    [("c2", torch.bfloat16, (0, 5)), ("c4", torch.bfloat16, (0, 23)), ("c1", torch.float32, (1,)),
+     ("c1", torch.bfloat16, (0,)), ("c3", torch.bfloat16, (1,)), ("bevformer-1l", torch.float32, (0,))],
+)
+def test_baseline_sizes_match_oracle_on_whole_images(cuda_device, config, dtype, images):
+    """The full batched launch at the BASELINE size, then every element of
+    whole camera images (all queries, all heads) against the C oracle,
+    grad_value included: dense images are where many samples of different
+    queries land on one pixel row and the backward's folded / merged
+    reductions meet."""
+    cfg = cases.CONFIGS[config]
+    inp = cases.make_inputs(cfg, dtype=dtype, device=cuda_device)
+    out, grads = _c_abi_fwd_bwd(inp, dtype)
+    torch.cuda.synchronize()
+    tol = FP32_TOL if dtype == torch.float32 else BF16_TOL
+    for b in images:
+        _image_check(inp, out, grads, b, tol, config)
+
+
+def test_c0_full_size_matches_oracle_everywhere(cuda_device):
+    """Config 0 at its stated size (Lin = Lq = 1360, fp32): every output and
+    gradient element, through the public autograd op and through the C-ABI."""
+    cfg = cases.CONFIGS["c0"]
+    inp = cases.make_inputs(cfg, dtype=torch.float32, device=cuda_device)
+    out, grads = _c_abi_fwd_bwd(inp, torch.float32)
+    torch.cuda.synchronize()
+    _image_check(inp, out, grads, 0, FP32_TOL, "c0")
+    tensors = [inp[k].clone().requires_grad_(inp[k].dtype.is_floating_point) for k in INPUTS]
+    o, gv, gl, gw = _fwd_bwd(tensors, inp["grad_output"])
+    torch.testing.assert_close(o, out, rtol=0, atol=0)
+    for got, want, name in ((gv, grads[0], "grad_value"), (gl, grads[1], "grad_loc"), (gw, grads[2], "grad_w")):
+        torch.testing.assert_close(got, want, rtol=FP32_TOL, atol=FP32_TOL, msg=lambda m, name=name: f"c0 {name}: {m}")
+
+
 def test_c4_batch_slices_equal_the_whole_and_grad_value_is_additive(cuda_device):
     """Size-independent properties at the full c4 size (B=48, bf16): per-camera
     slices reproduce the batched call exactly (forward, grad_loc, grad_w) and
