@@ -63,6 +63,16 @@ namespace msda {
 #ifndef MSDA_BWD_DEDUP
 #define MSDA_BWD_DEDUP 1
 #endif
+// 1: repeated corner rows fold through a per-group hash table in shared
+// memory (fold_rows_hashed) instead of a scan over all lower entries.
+#ifndef MSDA_BWD_HASH_FOLD
+#define MSDA_BWD_HASH_FOLD 1
+#endif
+// 1: the REDs of the lane-pair kernel are predicated instead of branched
+// around (a warp's four groups disagree on which entries need one).
+#ifndef MSDA_BWD_PRED_RED
+#define MSDA_BWD_PRED_RED 1
+#endif
 // 1: the lane-pair kernel also takes bf16 head-rows of at most 4 samples.
 #ifndef MSDA_PAIR_SHORT
 #define MSDA_PAIR_SHORT 1
@@ -213,19 +223,6 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
 //    writes grad_w / grad_loc: no transpose reduction, no geometry per lane;
 //  - REDs: every lane sends its 4-channel slice of (sum of w_k a) * g for each
 //    first-occurrence corner row (whole 128-byte lines per group for D = 32).
-template <typename T, int kCPL>
-struct PairShape {
-  static constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte chunk
-  static constexpr int kChannels = 2 * kCPL * kPer16;              // D
-  static constexpr int G = kChannels / 4;                          // lanes per head-row
-  static constexpr int kPairs16 = kPer16 / 2;                      // fp32 pairs per chunk
-#ifndef MSDA_PAIR_CORNERS
-#define MSDA_PAIR_CORNERS 1
-#endif
-  // corner gathers issued together (register budget: kCPL * 4 words each; at
-  // 64 registers one corner at a time measured fastest for D = 32)
-  static constexpr int kCornersInFlight = kCPL == 1 ? 4 : (kCPL == 2 ? MSDA_PAIR_CORNERS : 1);
-};
 
 // CTAs per SM the lane-pair kernel's register budget is sized for (4: 64
 // registers, 32 resident warps; 8.60 -> 8.06 ms for the c4 backward against 3).
@@ -248,10 +245,12 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
   constexpr int kPasses = Cs / kPerPass > 0 ? Cs / kPerPass : 1;
   constexpr int kGroups = kCtaThreads / G;
   constexpr int kSlots = Cs + 1;
+  constexpr int kHashSlots = 8 * Cs;  // >= 2 * (4 Cs entries), a power of two
   extern __shared__ Level levels[];
   __shared__ int4 s_row[kGroups * kSlots];
   __shared__ float4 s_wa[kGroups * kSlots];
   __shared__ float4 s_geo[kGroups * kSlots];
+  __shared__ __align__(16) int s_hash[MSDA_BWD_HASH_FOLD ? kGroups * kHashSlots : 4];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
@@ -310,9 +309,16 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
       }
       __syncwarp();
 #if MSDA_BWD_DEDUP
-      if constexpr (kScatter)
+      if constexpr (kScatter) {
+#if MSDA_BWD_HASH_FOLD
+        fold_rows_hashed<G, 4 * Cs, kHashSlots>(reinterpret_cast<const int*>(s_row + base),
+                                                reinterpret_cast<float*>(s_wa + base),
+                                                s_hash + (threadIdx.x / G) * kHashSlots, sub);
+#else
         fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(s_row + base),
                                       reinterpret_cast<float*>(s_wa + base), sub);
+#endif
+      }
 #endif
 #pragma unroll 1
       for (int p = 0; p < kPasses; ++p) {
@@ -381,9 +387,18 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
             const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
             const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
+            for (int k = 0; k < 4; ++k) {
+#if MSDA_BWD_PRED_RED
+              const float2 w2 = make_float2(wa[k], wa[k]);
+              const float2 lo = fmul2(w2, gr[0]), hi = fmul2(w2, gr[1]);
+              red_add_v4_if(rows[k] >= 0 && wa[k] != 0.0f,
+                            gbase + static_cast<int64_t>(rows[k] >= 0 ? rows[k] : 0) * row_stride, lo.x, lo.y,
+                            hi.x, hi.y);
+#else
               if (rows[k] >= 0 && wa[k] != 0.0f)
                 scatter_slice<2>(gbase + static_cast<int64_t>(rows[k]) * row_stride, wa[k], gr);
+#endif
+            }
           }
         }
       }

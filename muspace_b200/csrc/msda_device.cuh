@@ -213,6 +213,13 @@ __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
 __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
+// The same RED under a predicate (no branch: lanes of a warp that disagree on
+// `on` do not split the warp).
+__device__ __forceinline__ void red_add_v4_if(bool on, float* p, float a, float b, float c, float d) {
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.u32 q, %5, 0;\n @q red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n}" ::"l"(p),
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"(static_cast<unsigned>(on)));
+}
 
 // ---------------------------------------------------------------------------
 // level table
@@ -374,6 +381,66 @@ __device__ __forceinline__ void fold_repeated_rows(const int* row, float* wa, in
   }
   __syncwarp();
 }
+
+// The same fold through a per-group hash table in shared memory (kSlots ints,
+// a power of two >= 2 kEnt): every entry with a RED due claims its row's slot
+// with a compare-and-swap; an entry that finds the slot held by an entry of
+// the same row moves its wa there, one that finds another row (a hash
+// collision) keeps its own RED. The owner of a row is whichever entry claimed
+// it first, so the fold costs a few instructions per entry instead of a scan
+// over all lower entries. Movers are never owners, so no entry is read while
+// another lane adds into it.
+template <int G, int kEnt, int kSlots>
+__device__ __forceinline__ void fold_rows_hashed(const int* row, float* wa, int* table, int sub) {
+  static_assert((kSlots & (kSlots - 1)) == 0 && kSlots >= 2 * kEnt, "table: a power of two, at least twice the entries");
+  constexpr int kPer = (kEnt + G - 1) / G;
+  constexpr int kShift = 32 - __builtin_ctz(kSlots);
+#pragma unroll
+  for (int t = sub * 4; t < kSlots; t += G * 4) *reinterpret_cast<int4*>(table + t) = make_int4(-1, -1, -1, -1);
+  __syncwarp();
+  int owner[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = sub + j * G;
+    owner[j] = e;
+    if (e < kEnt) {
+      const int r = row[e];
+      if (r >= 0 && wa[e] != 0.0f) {
+        const int slot = static_cast<int>((static_cast<uint32_t>(r) * 2654435761u) >> kShift);
+        const int held = atomicCAS(table + slot, -1, e);
+        if (held >= 0 && row[held] == r) owner[j] = held;
+      }
+    }
+  }
+  __syncwarp();  // every claim is settled before any wa moves
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = sub + j * G;
+    if (owner[j] != e) {
+      atomicAdd(wa + owner[j], wa[e]);
+      wa[e] = 0.0f;
+    }
+  }
+  __syncwarp();
+}
+
+// Lane layout of the lane-pair backward kernels (msda_backward.cu,
+// msda_merge.cu): a head-row of D channels is 2 kCPL 16-byte chunks; lane h of
+// a pair holds chunks h, h + 2, ... for the corner dots, and G = D / 4 lanes
+// per head-row each own a 4-channel fp32 slice of the gradients.
+template <typename T, int kCPL>
+struct PairShape {
+  static constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte chunk
+  static constexpr int kChannels = 2 * kCPL * kPer16;              // D
+  static constexpr int G = kChannels / 4;                          // lanes per head-row
+  static constexpr int kPairs16 = kPer16 / 2;                      // fp32 pairs per chunk
+#ifndef MSDA_PAIR_CORNERS
+#define MSDA_PAIR_CORNERS 1
+#endif
+  // corner gathers issued together (register budget: kCPL * 4 words each; at
+  // 64 registers one corner at a time measured fastest for D = 32)
+  static constexpr int kCornersInFlight = kCPL == 1 ? 4 : (kCPL == 2 ? MSDA_PAIR_CORNERS : 1);
+};
 
 // ---------------------------------------------------------------------------
 // lane-group reductions and gradient scatter
