@@ -104,7 +104,8 @@ def _peaks() -> tuple[float, str]:
 # per 8-lane group (whole lines), measured on this pool's B200s (6.34-6.39
 # TB/s over 296-1184 CTAs); bulk reductions from shared memory reached less.
 RED_PEAK_GBS = 6390.0
-RED_PEAK_SOURCE = "measured: red.global.add.v4.f32, 128-byte lines into an L2-resident region (B200)"
+RED_PEAK_SOURCE = ("measured: red.global.add.v4.f32, 128-byte lines into an L2-resident region (B200; method and "
+                   "results in profiles/red_path_microbenchmarks.md)")
 
 
 def _red_bytes(kernel: str, launch_units: float):
