@@ -68,6 +68,7 @@ struct Shape {
   static constexpr int kBwdChunk = G < 8 ? kChunk : 8;
   static constexpr int kBwdStager = G / kBwdChunk;
   static constexpr int kSlots = kBwdChunk + 1;  // + padding against bank conflicts between groups
+  static constexpr int kHashSlots = kBwdChunk >= 8 ? 64 : (kBwdChunk >= 4 ? 32 : (kBwdChunk >= 2 ? 16 : 8));
 };
 
 // Per-group shared memory.
@@ -78,6 +79,7 @@ struct GroupSmem {
   int4 row[Shape<G>::kSlots];
   float4 wa[Shape<G>::kSlots];
   float4 geo[Shape<G>::kSlots];  // du, dv, attention weight, entry (int bits)
+  alignas(16) int hash[Shape<G>::kHashSlots];  // the backward's row fold
 };
 
 struct Cell {
@@ -257,12 +259,23 @@ __device__ __forceinline__ float4 sum_item(const Dims& d, const Map* maps, const
 #ifndef FSCA_FWD_MINBLOCKS
 #define FSCA_FWD_MINBLOCKS 4
 #endif
+// (backward at 4: 64 registers, 4 CTAs/SM; 1.371 -> 1.266 ms at BEVFormer-base
+// sizes against the compiler's own 80 registers)
 #ifndef FSCA_BWD_MINBLOCKS
-#define FSCA_BWD_MINBLOCKS 0
+#define FSCA_BWD_MINBLOCKS 4
 #endif
 // 1: fold repeated corner rows of a staged chunk before the backward's REDs.
 #ifndef FSCA_BWD_FOLD
 #define FSCA_BWD_FOLD 1
+#endif
+// 1: the fold goes through a per-group hash table (msda::fold_rows_hashed)
+// instead of a scan over all lower entries.
+#ifndef FSCA_BWD_HASH_FOLD
+#define FSCA_BWD_HASH_FOLD 1
+#endif
+// 1: the backward's REDs are predicated instead of branched around.
+#ifndef FSCA_BWD_PRED_RED
+#define FSCA_BWD_PRED_RED 1
 #endif
 #if FSCA_FWD_MINBLOCKS > 0
 #define FSCA_FWD_BOUNDS(G) __launch_bounds__(Shape<G>::kThreads, FSCA_FWD_MINBLOCKS)
@@ -396,7 +409,10 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
       // samples of one level around the heights of a camera share corner rows
       // (at the coarse levels most of them): each row's w * a is summed into
       // its first occurrence in the chunk and only those rows are sent
-#if FSCA_BWD_FOLD
+#if FSCA_BWD_FOLD && FSCA_BWD_HASH_FOLD
+      msda::fold_rows_hashed<G, 4 * Cs, Sh::kHashSlots>(reinterpret_cast<const int*>(sm.row),
+                                                       reinterpret_cast<float*>(sm.wa), sm.hash, sub);
+#elif FSCA_BWD_FOLD
       msda::fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(sm.row),
                                           reinterpret_cast<float*>(sm.wa), sub);
 #endif
@@ -422,8 +438,14 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
               pay = make_float4(keep(raw.x, pay.x), keep(raw.y, pay.y), keep(raw.z, pay.z), keep(raw.w, pay.w));
             }
             t[i][k] = dot;
+#if FSCA_BWD_PRED_RED
+            msda::red_add_v4_if(rows[k] >= 0 && wa[k] != 0.0f,
+                                gvb + static_cast<int64_t>(rows[k] >= 0 ? rows[k] : 0) * d.channels, pay.x, pay.y,
+                                pay.z, pay.w);
+#else
             if (rows[k] >= 0 && wa[k] != 0.0f)
               msda::red_add_v4(gvb + static_cast<int64_t>(rows[k]) * d.channels, pay.x, pay.y, pay.z, pay.w);
+#endif
           }
         }
         msda::reduce_to_stagers<G, C>(t, sub);
