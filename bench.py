@@ -21,7 +21,10 @@ data path), and the time is the slowest rank's; ``--scaling weak`` gives every
 rank its own 48-image shard instead. ``--variant query`` runs the bs=1 form: one
 6-camera sample, queries split across ranks, value replicated, fp32
 ``grad_value`` reduce-scattered with NCCL; its ``kernels_ms`` separate the
-kernels from the reduce-scatter. ``--protocol reference`` times the reference's
+kernels from the reduce-scatter. At N = 1 the line also carries
+``other_workloads``: 10-step device times of the other configs (c0-c3, the
+reference's ``bevformer-1l``) and of the ops built next to MSDA.
+``--protocol reference`` times the reference's
 published-case protocol instead (20 warm-ups, 5 repeats x 100 launches, median;
 ``benchmarks/_harness.py:226-260``) for both the reference's timed closure and
 this build's step, next to the published figures.
@@ -69,6 +72,8 @@ def parse_args():
                    help="--variant query: backward and grad_value reduce-scatter per camera image, overlapped")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-other-workloads", action="store_true",
+                   help="skip the short device-time runs of the other configs and ops (N = 1 only)")
     p.add_argument("--quiet", action="store_true", help="print only the JSON line")
     p.add_argument("--protocol", choices=("contract", "reference"), default="contract",
                    help="reference: the reference's published-case timing protocol (p50 of 5 x 100 launches)")
@@ -434,7 +439,55 @@ def run_b200(args, cfg, dtype, rank, world, device):
             "payload_bytes": int(red), "peak_source": RED_PEAK_SOURCE}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, dtype)
+    if world == 1 and not args.no_other_workloads:
+        line["other_workloads"] = other_workloads(device)
     return line
+
+
+# The other BASELINE configs and the reference's published case, each as the
+# headline's step (forward, grad_value fill, backward) on device-resident inputs.
+OTHER_CONFIGS = (("c0", torch.float32), ("c1", torch.float32), ("c1", torch.bfloat16), ("c2", torch.bfloat16),
+                 ("c3", torch.bfloat16), ("bevformer-1l", torch.float32), ("bevformer-1l", torch.bfloat16))
+OTHER_OPS = ("deformable_aggregation", "flash_sca", "sca_scatter")
+
+
+def _time_steps(step, steps=10, warmup=3, phases=None):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def other_workloads(device):
+    """Device time per step of every other config (c0-c3, bevformer-1l) and of
+    the ops built next to MSDA, 10 timed steps after 3 warm-ups each (inputs
+    resident on the device, so their own bench lines' e2e and CPU legs are
+    left out): the configs as the headline's step, the ops as their own
+    ``--op`` step."""
+    out = {}
+    for name, dtype in OTHER_CONFIGS:
+        cfg = cases.CONFIGS[name]
+        inp = cases.make_inputs(cfg, dtype=dtype, device=device)
+        step = Step(inp, dtype, device)
+        ms = _time_steps(step)
+        nbytes = cases.compulsory_bytes(cfg, dtype)["total"]
+        out[f"{name}/{_dtype_tag(dtype)}"] = {"ms_per_step": round(ms, 4),
+                                              "gbs": round(nbytes / (ms / 1e3) / 1e9, 1)}
+        del inp, step
+        torch.cuda.empty_cache()
+    for op in OTHER_OPS:
+        w = OpWorkload(op, device)
+        ms = _time_steps(w.step)
+        out[op] = {"ms_per_step": round(ms, 4), "gbs": round(w.bytes / (ms / 1e3) / 1e9, 1)}
+        del w
+        torch.cuda.empty_cache()
+    return out
 
 
 class E2ESlot:

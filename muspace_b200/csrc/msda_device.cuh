@@ -177,18 +177,27 @@ __device__ __forceinline__ Words<kBytes / 4> ld_stream_words(const void* p, uint
 __device__ __forceinline__ void st16(void* p, const uint4& v) { *reinterpret_cast<uint4*>(p) = v; }
 
 // Two independent fp32 FMAs in one instruction (sm_100 fma.rn.f32x2); each
-// lane rounds exactly like fmaf.
+// lane rounds exactly like fmaf. 1: through the compiler's own sm_100
+// intrinsic (__ffma2_rn / __fmul2_rn), which it schedules and allocates
+// registers for; 0: inline PTX.
+#ifndef MSDA_NATIVE_F2
+#define MSDA_NATIVE_F2 1
+#endif
 union F2 {
   float2 f;
   unsigned long long u;
 };
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+#if MSDA_NATIVE_F2
+  return __ffma2_rn(a, b, c);
+#else
   F2 x, y, z, r;
   x.f = a;
   y.f = b;
   z.f = c;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.u) : "l"(x.u), "l"(y.u), "l"(z.u));
   return r.f;
+#endif
 }
 // acc.x += lo(g) * lo(v), acc.y += hi(g) * hi(v) for two words of two bf16
 // channels each, in fp32 (sm_100 mixed-precision FMA: the bf16 x bf16 product
@@ -522,11 +531,15 @@ __device__ __forceinline__ void reduce_to_stagers(float (&t)[C][4], int sub) {
 
 // Two fp32 products in one instruction (sm_100 mul.rn.f32x2).
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+#if MSDA_NATIVE_F2
+  return __fmul2_rn(a, b);
+#else
   F2 x, y, r;
   x.f = a;
   y.f = b;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.u) : "l"(x.u), "l"(y.u));
   return r.f;
+#endif
 }
 
 // grad_value[corner row] += wa * g over a lane's own channel slice
