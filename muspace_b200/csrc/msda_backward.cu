@@ -73,6 +73,11 @@ namespace msda {
 #ifndef MSDA_BWD_PRED_RED
 #define MSDA_BWD_PRED_RED 1
 #endif
+// 1: bf16 D = 32 forms a sample's dots with four lanes (one 16-byte chunk of
+// each corner row per lane) instead of a lane pair (two chunks per lane).
+#ifndef MSDA_BWD_QUAD
+#define MSDA_BWD_QUAD 1
+#endif
 // 1: the lane-pair kernel also takes bf16 head-rows of at most 4 samples.
 #ifndef MSDA_PAIR_SHORT
 #define MSDA_PAIR_SHORT 1
@@ -230,18 +235,18 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
 #define MSDA_PAIR_MINBLOCKS 4
 #endif
 
-template <typename T, int kCPL, int kStageMax, bool kScatter>
+template <typename T, int kCPL, int kStageMax, bool kScatter, int kLPS = 2>
 __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pair_kernel(
     Dims d, const T* __restrict__ value, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
     const T* __restrict__ loc, const T* __restrict__ weight, const T* __restrict__ grad_out,
     float* __restrict__ grad_value, float* __restrict__ grad_loc, float* __restrict__ grad_weight,
     const int* __restrict__ order) {
-  using Sh = PairShape<T, kCPL>;
+  using Sh = PairShape<T, kCPL, kLPS>;
   using S16 = Slice<T, 16>;
   constexpr int G = Sh::G;
   constexpr int Cs = G < kStageMax ? G : kStageMax;  // samples staged per chunk
   constexpr int kStage = G / Cs;                     // stager lanes: sub % kStage == 0
-  constexpr int kPerPass = G / 2;                     // samples whose dots run at once
+  constexpr int kPerPass = G / kLPS;                  // samples whose dots run at once
   constexpr int kPasses = Cs / kPerPass > 0 ? Cs / kPerPass : 1;
   constexpr int kGroups = kCtaThreads / G;
   constexpr int kSlots = Cs + 1;
@@ -254,7 +259,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
-  const int half = sub & 1, member = sub >> 1;  // lane of the pair, pair within the group
+  const int lq = sub % kLPS, member = sub / kLPS;  // lane of the sample's lanes, sample within the pass
   const int base = (threadIdx.x / G) * kSlots;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int row_stride = d.heads * d.channels;
@@ -275,7 +280,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
     const T* wp = weight + it * samples;
     const T* grow = grad_out + it * d.channels;
 
-    // grad_output in the pair layout (chunks half, half + 2, ...) and as this
+    // grad_output in the dot layout (chunks lq, lq + kLPS, ...) and as this
     // lane's 4-channel slice for the REDs
     // bf16 with the mixed-precision FMA keeps grad_output as raw words
     constexpr bool kMixed = sizeof(T) == 2 && MSDA_BWD_MIXED_FMA;
@@ -285,7 +290,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
       const uint64_t policy = evict_first_policy();
 #pragma unroll
       for (int j = 0; j < kCPL; ++j) {
-        graw[j] = ld_stream_words<16>(grow + (2 * j + half) * Sh::kPer16, policy);
+        graw[j] = ld_stream_words<16>(grow + (j * kLPS + lq) * Sh::kPer16, policy);
         if constexpr (!kMixed) {
 #pragma unroll
           for (int q = 0; q < Sh::kPairs16; ++q) ga[j][q] = S16::pair(graw[j], q);
@@ -337,7 +342,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
 #pragma unroll
               for (int j = 0; j < kCPL; ++j)
                 raw[kk][j] = row >= 0 ? ldg_words<16>(vrow + static_cast<int64_t>(row) * row_stride +
-                                                      (2 * j + half) * Sh::kPer16)
+                                                      (j * kLPS + lq) * Sh::kPer16)
                                       : zero_words<4>();
             }
 #pragma unroll
@@ -357,9 +362,11 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
             }
           }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], 1);
+          for (int m = 1; m < kLPS; m <<= 1)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], m);
           const int s = s0 + i;
-          if (half == 0 && live && s < samples) {
+          if (lq == 0 && live && s < samples) {
             const float4 geo = s_geo[base + i];
             float gw = 0.0f, gx = 0.0f, gy = 0.0f;
             if (geo.w != 0.0f) {
@@ -497,18 +504,18 @@ static cudaError_t launch_backward_lanes(int g, const Dims& d, const Args& a, cu
   }
 }
 
-template <typename T, int kCPL>
+template <typename T, int kCPL, int kLPS = 2>
 static cudaError_t launch_backward_pair(const Dims& d, const Args& a, cudaStream_t stream) {
-  constexpr int G = PairShape<T, kCPL>::G;
+  constexpr int G = PairShape<T, kCPL, kLPS>::G;
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int64_t groups_per_cta = kCtaThreads / G;
   const int64_t blocks = (items + groups_per_cta - 1) / groups_per_cta;
   const int grid = static_cast<int>(blocks < grid_cap() ? blocks : grid_cap());
   const bool short_rows = d.levels * d.points <= 4;
-  auto kernel = short_rows ? (a.skip_grad_value ? backward_pair_kernel<T, kCPL, 4, false>
-                                                : backward_pair_kernel<T, kCPL, 4, true>)
-                           : (a.skip_grad_value ? backward_pair_kernel<T, kCPL, 8, false>
-                                                : backward_pair_kernel<T, kCPL, 8, true>);
+  auto kernel = short_rows ? (a.skip_grad_value ? backward_pair_kernel<T, kCPL, 4, false, kLPS>
+                                                : backward_pair_kernel<T, kCPL, 4, true, kLPS>)
+                           : (a.skip_grad_value ? backward_pair_kernel<T, kCPL, 8, false, kLPS>
+                                                : backward_pair_kernel<T, kCPL, 8, true, kLPS>);
   kernel<<<grid, kCtaThreads, level_smem(d), stream>>>(
       d, static_cast<const T*>(a.value), a.shapes, a.starts, static_cast<const T*>(a.loc),
       static_cast<const T*>(a.weight), static_cast<const T*>(a.grad_out), a.grad_value, a.grad_loc, a.grad_weight,
@@ -529,7 +536,10 @@ static cudaError_t launch_backward_t(const Dims& d, const Args& a, cudaStream_t 
         vec_lanes(d.channels, 4, 16, a) != 0) {
       switch (d.channels * static_cast<int>(sizeof(T)) / 32) {
         case 1: return launch_backward_pair<T, 1>(d, a, stream);
-        case 2: return launch_backward_pair<T, 2>(d, a, stream);
+        case 2:
+          // D = 32: four lanes of one 16-byte chunk each per sample (a gather instruction
+          // reads 64 bytes of each row it touches), or two lanes of two chunks
+          return MSDA_BWD_QUAD ? launch_backward_pair<T, 1, 4>(d, a, stream) : launch_backward_pair<T, 2>(d, a, stream);
         default: break;
       }
     }

@@ -433,14 +433,15 @@ __device__ __forceinline__ void fold_rows_hashed(const int* row, float* wa, int*
   __syncwarp();
 }
 
-// Lane layout of the lane-pair backward kernels (msda_backward.cu,
-// msda_merge.cu): a head-row of D channels is 2 kCPL 16-byte chunks; lane h of
-// a pair holds chunks h, h + 2, ... for the corner dots, and G = D / 4 lanes
-// per head-row each own a 4-channel fp32 slice of the gradients.
-template <typename T, int kCPL>
+// Lane layout of the lane-pair / lane-quad backward kernels (msda_backward.cu):
+// a head-row of D channels is kLPS x kCPL 16-byte chunks; a sample's dots are
+// formed by kLPS lanes, lane q holding chunks q, q + kLPS, ... of the corner
+// rows, and G = D / 4 lanes per head-row each own a 4-channel fp32 slice of
+// the gradients.
+template <typename T, int kCPL, int kLPS = 2>
 struct PairShape {
   static constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16-byte chunk
-  static constexpr int kChannels = 2 * kCPL * kPer16;              // D
+  static constexpr int kChannels = kLPS * kCPL * kPer16;           // D
   static constexpr int G = kChannels / 4;                          // lanes per head-row
   static constexpr int kPairs16 = kPer16 / 2;                      // fp32 pairs per chunk
 #ifndef MSDA_PAIR_CORNERS
