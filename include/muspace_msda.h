@@ -377,6 +377,14 @@ MSDA_API int flash_bevpool_sca_backward(const DLTensor *out_grad, const DLTensor
  * reference raised it as a TVM-FFI exception (csrc/ffi/tensor_utils.hpp:13-34). */
 MSDA_API const char *msda_last_error(void);
 
+/* Waits of the staged bf16 forward (opt-in through MUSPACE_FWD_STAGED=1: the
+ * kernel that copies each head's smallest levels into shared memory with TMA;
+ * measured slower than the default forward) that gave up on the copies on the current
+ * device since the library loaded; such a thread reads the rows from global
+ * memory instead, so results are unchanged. A diagnostic: 0 is expected.
+ * Returns MSDA_STATUS_CUDA_ERROR when the counter cannot be read. */
+MSDA_API int msda_stage_wait_timeouts(unsigned int *count);
+
 /* Library version string, "<major>.<minor>.<patch>". */
 MSDA_API const char *msda_version(void);
 

@@ -21,7 +21,7 @@ PACKAGE = Path(__file__).resolve().parent
 CSRC = PACKAGE / "csrc"
 INCLUDE = PACKAGE.parent / "include"
 LIBRARY = PACKAGE / "native" / "libmuspace_ops.so"
-SOURCES = ("msda_capi.cpp", "msda_forward.cu", "msda_backward.cu", "msda_bucketed.cu", "msda_noalloc.cu",
+SOURCES = ("msda_capi.cpp", "msda_forward.cu", "msda_staged.cu", "msda_backward.cu", "msda_bucketed.cu", "msda_noalloc.cu",
            "msda_deterministic.cu", "deform_agg.cu", "flash_sca.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 

@@ -788,6 +788,15 @@ int flash_bevpool_sca_backward(const DLTensor* out_grad, const DLTensor* value, 
 
 const char* msda_last_error(void) { return g_last_error.c_str(); }
 
+int msda_stage_wait_timeouts(unsigned int* count) {
+  return guarded([&] {
+    require(count != nullptr, "count is null");
+    const unsigned int v = msda::staged_wait_timeouts();
+    if (v == ~0u) fail(MSDA_STATUS_CUDA_ERROR, "the staged forward's wait counter could not be read");
+    *count = v;
+  });
+}
+
 const char* msda_version(void) { return "0.1.0"; }
 
 }  // extern "C"

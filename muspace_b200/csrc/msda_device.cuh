@@ -230,6 +230,28 @@ __device__ __forceinline__ void red_add_v4_if(bool on, float* p, float a, float 
       "f"(a), "f"(b), "f"(c), "f"(d), "r"(static_cast<unsigned>(on)));
 }
 
+// Whether every channel pair of acc is finite.
+template <int kPairs>
+__device__ __forceinline__ bool finite_pairs(const float2 (&acc)[kPairs]) {
+  bool ok = true;
+#pragma unroll
+  for (int q = 0; q < kPairs; ++q) ok = ok && fabsf(acc[q].x) <= 3.402823466e+38f && fabsf(acc[q].y) <= 3.402823466e+38f;
+  return ok;
+}
+
+// Stores a lane's kBytes slice of channels (fp32 pairs) in the storage dtype.
+template <typename T, int kBytes>
+__device__ __forceinline__ void store_slice(T* dst, const float2 (&acc)[Slice<T, kBytes>::kPairs]) {
+  constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16 bytes
+#pragma unroll
+  for (int h = 0; h < kBytes / 16; ++h) {
+    float f[kPer16];
+#pragma unroll
+    for (int q = 0; q < kPer16 / 2; ++q) f[2 * q] = acc[h * kPer16 / 2 + q].x, f[2 * q + 1] = acc[h * kPer16 / 2 + q].y;
+    st16(dst + h * kPer16, Vec16<T>::pack(f));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // level table
 // ---------------------------------------------------------------------------

@@ -91,15 +91,6 @@ __device__ __forceinline__ void substitute_outside_corners(int4* row, float4* wa
   *wa = w;
 }
 
-// Whether every channel pair of acc is finite.
-template <int kPairs>
-__device__ __forceinline__ bool finite_pairs(const float2 (&acc)[kPairs]) {
-  bool ok = true;
-#pragma unroll
-  for (int q = 0; q < kPairs; ++q) ok = ok && fabsf(acc[q].x) <= 3.402823466e+38f && fabsf(acc[q].y) <= 3.402823466e+38f;
-  return ok;
-}
-
 // acc (this lane's channel pairs) += sum over the head-row's samples of
 // sum_k (w_k a) v_k. vbase points at the lane's channel slice of pixel 0 of
 // the head's value map; lp / wp at the head-row's locations / weights; row /
@@ -155,19 +146,6 @@ __device__ __forceinline__ void gather_head_row(const Level* levels, int points,
       }
     }
     __syncwarp();
-  }
-}
-
-// Stores / loads a lane's kBytes slice of channels as fp32 pairs.
-template <typename T, int kBytes>
-__device__ __forceinline__ void store_slice(T* dst, const float2 (&acc)[Slice<T, kBytes>::kPairs]) {
-  constexpr int kPer16 = 16 / static_cast<int>(sizeof(T));  // channels per 16 bytes
-#pragma unroll
-  for (int h = 0; h < kBytes / 16; ++h) {
-    float f[kPer16];
-#pragma unroll
-    for (int q = 0; q < kPer16 / 2; ++q) f[2 * q] = acc[h * kPer16 / 2 + q].x, f[2 * q + 1] = acc[h * kPer16 / 2 + q].y;
-    st16(dst + h * kPer16, Vec16<T>::pack(f));
   }
 }
 
@@ -359,6 +337,11 @@ static cudaError_t launch_forward_lanes(int g, const Dims& d, const Args& a, cud
 
 template <typename T>
 static cudaError_t launch_forward_t(const Dims& d, const Args& a, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    bool staged = false;
+    const cudaError_t e = launch_forward_staged(d, a, stream, &staged);
+    if (staged || e != cudaSuccess) return e;
+  }
   constexpr int kWide = sizeof(T) == 2 ? MSDA_FWD_LANE_BYTES_BF16 : MSDA_FWD_LANE_BYTES_F32;
   if constexpr (kWide == 32) {
     if (const int g = vec_lanes(d.channels, sizeof(T), 32, a)) return launch_forward_lanes<T, 32>(g, d, a, stream);

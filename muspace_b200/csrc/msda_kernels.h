@@ -105,6 +105,13 @@ cudaError_t static_scratch_address(void** out);
 cudaError_t launch_forward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 cudaError_t launch_backward_rowwise(DType dtype, const Dims& d, const Args& a, cudaStream_t stream);
 
+// bf16 D = 32 forward with the smallest levels staged in shared memory by TMA
+// (msda_staged.cu; opt-in, MUSPACE_FWD_STAGED=1); *used = false when it is off
+// or the call does not suit it, and the row-wise kernels take the call.
+cudaError_t launch_forward_staged(const Dims& d, const Args& a, cudaStream_t stream, bool* used);
+// Copy waits of the staged forward that gave up so far (this device; ~0u when
+// it cannot be read).
+unsigned int staged_wait_timeouts();
 // Fused MSDA forward + rebatch scatter + count normalisation for one camera
 // (msda_forward.cu); d describes the rebatched call (batch = B * cams,
 // queries = max_len). cudaErrorInvalidValue when the channel count has no
