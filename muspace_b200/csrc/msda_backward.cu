@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
   __shared__ int4 s_row[kGroups * kSlots];
   __shared__ float4 s_wa[kGroups * kSlots];
   __shared__ float4 s_geo[kGroups * kSlots];
+  __shared__ float4 s_dots[kGroups * kSlots];
   __shared__ __align__(16) int s_hash[MSDA_BWD_HASH_FOLD ? kGroups * kHashSlots : 4];
   stage_levels(levels, shapes, starts, d);
 
@@ -307,10 +308,15 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
 
     for (int s0 = 0; s0 < samples; s0 += Cs) {
       if (sub % kStage == 0) {
+        // geometry for the gradient formula: (lh, lw, W a, H a), lh = -1 for
+        // a sample with no corner inside its level
         const int i = sub / kStage;
         float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo);
-        s_geo[base + i] = geo;
+        float2 wh = make_float2(0.0f, 0.0f);
+        const bool valid =
+            stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo, &wh);
+        s_geo[base + i] =
+            valid ? make_float4(geo.x, geo.y, wh.x * geo.z, wh.y * geo.z) : make_float4(-1.0f, 0.0f, 0.0f, 0.0f);
       }
       __syncwarp();
 #if MSDA_BWD_DEDUP
@@ -365,23 +371,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
           for (int m = 1; m < kLPS; m <<= 1)
 #pragma unroll
             for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], m);
-          const int s = s0 + i;
-          if (lq == 0 && live && s < samples) {
-            const float4 geo = s_geo[base + i];
-            float gw = 0.0f, gx = 0.0f, gy = 0.0f;
-            if (geo.w != 0.0f) {
-              const Level lv = levels[s / d.points];
-              const float lh = geo.x, lw = geo.y, a = geo.z;
-              const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
-              gw = __fmul_rn(hh, hw) * t[0] + __fmul_rn(hh, lw) * t[1] + __fmul_rn(lh, hw) * t[2] +
-                   __fmul_rn(lh, lw) * t[3];
-              gx = static_cast<float>(lv.width) * a * (hh * (t[1] - t[0]) + lh * (t[3] - t[2]));
-              gy = static_cast<float>(lv.height) * a * (hw * (t[2] - t[0]) + lw * (t[3] - t[1]));
-            }
-            const int64_t so = it * samples + s;
-            grad_weight[so] = gw;
-            *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(gx, gy);
-          }
+          if (lq == 0) s_dots[base + i] = make_float4(t[0], t[1], t[2], t[3]);
         }
         // REDs of the same samples by every lane's slice
         if constexpr (kScatter) {
@@ -407,6 +397,29 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
 #endif
             }
           }
+        }
+      }
+      __syncwarp();
+      // grad_w / grad_loc of the chunk: every stager lane takes its own sample
+      // (the whole chunk in one pass of the warp; the group's stores cover
+      // contiguous runs of grad_w and grad_loc)
+      if (sub % kStage == 0) {
+        const int i = sub / kStage;
+        const int s = s0 + i;
+        if (live && s < samples) {
+          const float4 geo = s_geo[base + i];
+          const float4 t = s_dots[base + i];
+          float gw = 0.0f, gx = 0.0f, gy = 0.0f;
+          if (geo.x >= 0.0f) {
+            const float lh = geo.x, lw = geo.y;
+            const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
+            gw = __fmul_rn(hh, hw) * t.x + __fmul_rn(hh, lw) * t.y + __fmul_rn(lh, hw) * t.z + __fmul_rn(lh, lw) * t.w;
+            gx = geo.z * (hh * (t.y - t.x) + lh * (t.w - t.z));
+            gy = geo.w * (hw * (t.z - t.x) + lw * (t.w - t.y));
+          }
+          const int64_t so = it * samples + s;
+          grad_weight[so] = gw;
+          *reinterpret_cast<float2*>(grad_loc + 2 * so) = make_float2(gx, gy);
         }
       }
       __syncwarp();  // the next chunk's staging overwrites the slots read above

@@ -337,11 +337,12 @@ struct Chunk {
 // four corner rows (-1 = outside the level, or no sample) and w_k * a in the
 // caller's shared slots. Returns whether the sample has a corner inside its
 // level, and, when geo is given, stores (lh, lw, a, 1) there for a valid
-// sample (the caller zeroes it), for the gradient formulas.
+// sample (the caller zeroes it), for the gradient formulas; when wh is given
+// too, the level's (W, H) as floats.
 template <typename T>
 __device__ __forceinline__ bool stage_sample(const Level* levels, int points, int samples, bool live, int s,
                                              const T* lp, const T* wp, int4* row_slot, float4* wa_slot,
-                                             float4* geo = nullptr) {
+                                             float4* geo = nullptr, float2* wh = nullptr) {
   int4 r = make_int4(-1, -1, -1, -1);
   float4 wa = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   bool valid = false;
@@ -355,6 +356,7 @@ __device__ __forceinline__ bool stage_sample(const Level* levels, int points, in
       r = make_int4(c.row[0], c.row[1], c.row[2], c.row[3]);
       wa = make_float4(c.w[0] * a, c.w[1] * a, c.w[2] * a, c.w[3] * a);
       if (geo) *geo = make_float4(c.lh, c.lw, a, 1.0f);
+      if (wh) *wh = make_float2(static_cast<float>(lv.width), static_cast<float>(lv.height));
     }
   }
   *row_slot = r;
