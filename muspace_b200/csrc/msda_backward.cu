@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
   __shared__ int4 s_row[kGroups * kSlots];
   __shared__ float4 s_wa[kGroups * kSlots];
   __shared__ float4 s_geo[kGroups * kSlots];
+  __shared__ float4 s_dots[kGroups * kSlots];
   stage_levels(levels, shapes, starts, d);
 
   const int sub = threadIdx.x % G;
@@ -146,12 +147,16 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
     }
 
     for (int s0 = 0; s0 < samples; s0 += Cs) {
-      // 1. stage
+      // 1. stage, with the geometry of the gradient formula: (lh, lw, W a, H a),
+      // lh = -1 for a sample with no corner inside its level
       if (sub % kStage == 0) {
         const int i = sub / kStage;
         float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo);
-        s_geo[base + i] = geo;
+        float2 wh = make_float2(0.0f, 0.0f);
+        const bool valid =
+            stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo, &wh);
+        s_geo[base + i] =
+            valid ? make_float4(geo.x, geo.y, wh.x * geo.z, wh.y * geo.z) : make_float4(-1.0f, 0.0f, 0.0f, 0.0f);
       }
       __syncwarp();
 #if MSDA_BWD_DEDUP
@@ -161,7 +166,7 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
                                       reinterpret_cast<float*>(s_wa + base), sub);
 #endif
       // 3. per sample: gathers, corner dots, the sample's REDs; per round the
-      // gradients of the locations / weights
+      // dots reach their sample's finishing lane
 #pragma unroll
       for (int r = 0; r < Cs / Cd; ++r) {
         float t[Cd][4];
@@ -191,20 +196,24 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
           }
         }
         reduce_to_stagers<G, Cd>(t, sub);
-        const int i = sub / kFin;
-        const int s = s0 + r * Cd + i;
-        if (sub % kFin == 0 && live && s < samples) {
-          const float4 geo = s_geo[base + r * Cd + i];
+        if (sub % kFin == 0) s_dots[base + r * Cd + sub / kFin] = make_float4(t[0][0], t[0][1], t[0][2], t[0][3]);
+      }
+      __syncwarp();
+      // 4. grad_w / grad_loc of the chunk: every stager lane takes its own
+      // sample (the whole chunk in one pass of the warp)
+      if (sub % kStage == 0) {
+        const int i = sub / kStage;
+        const int s = s0 + i;
+        if (live && s < samples) {
+          const float4 geo = s_geo[base + i];
+          const float4 t = s_dots[base + i];
           float gw = 0.0f, gx = 0.0f, gy = 0.0f;
-          if (geo.w != 0.0f) {
-            const Level lv = levels[s / d.points];
-            const float lh = geo.x, lw = geo.y, a = geo.z;
+          if (geo.x >= 0.0f) {
+            const float lh = geo.x, lw = geo.y;
             const float hh = __fsub_rn(1.0f, lh), hw = __fsub_rn(1.0f, lw);
-            const float* tt = t[0];
-            gw = __fmul_rn(hh, hw) * tt[0] + __fmul_rn(hh, lw) * tt[1] + __fmul_rn(lh, hw) * tt[2] +
-                 __fmul_rn(lh, lw) * tt[3];
-            gx = static_cast<float>(lv.width) * a * (hh * (tt[1] - tt[0]) + lh * (tt[3] - tt[2]));
-            gy = static_cast<float>(lv.height) * a * (hw * (tt[2] - tt[0]) + lw * (tt[3] - tt[1]));
+            gw = __fmul_rn(hh, hw) * t.x + __fmul_rn(hh, lw) * t.y + __fmul_rn(lh, hw) * t.z + __fmul_rn(lh, lw) * t.w;
+            gx = geo.z * (hh * (t.y - t.x) + lh * (t.w - t.z));
+            gy = geo.w * (hw * (t.z - t.x) + lw * (t.w - t.y));
           }
           const int64_t so = it * samples + s;
           grad_weight[so] = gw;
