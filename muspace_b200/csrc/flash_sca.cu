@@ -77,7 +77,7 @@ struct GroupSmem {
   int pair[kMaxPairs];
   float2 uv[kMaxPairs];  // projection / image size
   int4 row[Shape<G>::kSlots];
-  float4 wa[Shape<G>::kSlots];
+  float4 wa[Shape<G>::kSlots];   // w_k * a of each corner; in the backward, once a round's REDs are out, its dots
   float4 geo[Shape<G>::kSlots];  // du, dv, attention weight, entry (int bits)
   alignas(16) int hash[Shape<G>::kHashSlots];  // the backward's row fold
 };
@@ -449,18 +449,25 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
           }
         }
         msda::reduce_to_stagers<G, C>(t, sub);
-        const int i = sub / (G / C);
-        if (sub % (G / C) == 0 && live && s0 + c0 + i < samples) {
-          const float4 geo = sm.geo[c0 + i];
+        __syncwarp();  // the round's w * a slots are read; they take its dots
+        if (sub % (G / C) == 0) sm.wa[c0 + sub / (G / C)] = make_float4(t[0][0], t[0][1], t[0][2], t[0][3]);
+      }
+      __syncwarp();
+      // offset / weight gradients of the chunk: every stager lane takes its own
+      // sample (the whole chunk in one pass of the warp)
+      if (sub % Sh::kBwdStager == 0) {
+        const int i = sub / Sh::kBwdStager;
+        if (live && s0 + i < samples) {
+          const float4 geo = sm.geo[i];
           const float du = geo.x, dv = geo.y, weight = geo.z;
           const int e = __float_as_int(geo.w);
-          const float* tt = t[0];  // f00, f01, f10, f11 dots
+          const float4 tt = sm.wa[i];  // f00, f01, f10, f11 dots
           const float hu = 1.0f - du, hv = 1.0f - dv;
-          const float ds_du = hv * (tt[2] - tt[0]) + dv * (tt[3] - tt[1]);
-          const float ds_dv = hu * (tt[1] - tt[0]) + du * (tt[3] - tt[2]);
+          const float ds_du = hv * (tt.z - tt.x) + dv * (tt.w - tt.y);
+          const float ds_dv = hu * (tt.y - tt.x) + du * (tt.w - tt.z);
           atomicAdd(goff_item + 2 * e, weight * ds_du);
           atomicAdd(goff_item + 2 * e + 1, weight * ds_dv);
-          atomicAdd(gw_item + e, hu * hv * tt[0] + hu * dv * tt[1] + du * hv * tt[2] + du * dv * tt[3]);
+          atomicAdd(gw_item + e, hu * hv * tt.x + hu * dv * tt.y + du * hv * tt.z + du * dv * tt.w);
         }
       }
       __syncwarp();
