@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
         float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         float2 wh = make_float2(0.0f, 0.0f);
         const bool valid =
-            stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo, &wh);
+            stage_sample(levels, level_of(d), samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo, &wh);
         s_geo[base + i] =
             valid ? make_float4(geo.x, geo.y, wh.x * geo.z, wh.y * geo.z) : make_float4(-1.0f, 0.0f, 0.0f, 0.0f);
       }
@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
         float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         float2 wh = make_float2(0.0f, 0.0f);
         const bool valid =
-            stage_sample(levels, d.points, samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo, &wh);
+            stage_sample(levels, level_of(d), samples, live, s0 + i, lp, wp, s_row + base + i, s_wa + base + i, &geo, &wh);
         s_geo[base + i] =
             valid ? make_float4(geo.x, geo.y, wh.x * geo.z, wh.y * geo.z) : make_float4(-1.0f, 0.0f, 0.0f, 0.0f);
       }

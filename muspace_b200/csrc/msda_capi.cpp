@@ -93,7 +93,8 @@ void check_dims(const msda_dims_t& d) {
 msda::Dims to_kernel_dims(const msda_dims_t& d) {
   return msda::Dims{static_cast<int>(d.batch),   static_cast<int>(d.spatial_size), static_cast<int>(d.heads),
                     static_cast<int>(d.channels), static_cast<int>(d.levels),       static_cast<int>(d.queries),
-                    static_cast<int>(d.points)};
+                    static_cast<int>(d.points),
+                    msda::points_magic(static_cast<int>(d.levels), static_cast<int>(d.points))};
 }
 
 void check_launch(cudaError_t err, const char* what) {

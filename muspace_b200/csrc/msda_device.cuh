@@ -333,6 +333,18 @@ struct Chunk {
   static constexpr int kStagerStride = G / kSamples;
 };
 
+// The level of sample s of a head-row (samples are level-major, `points` per
+// level): a multiply-high by Dims::points_magic when the host set one, else a
+// division.
+struct LevelOf {
+  int points;
+  uint32_t magic;
+  __device__ __forceinline__ int operator()(int s) const {
+    return magic ? static_cast<int>(__umulhi(static_cast<uint32_t>(s), magic)) : s / points;
+  }
+};
+__device__ __forceinline__ LevelOf level_of(const Dims& d) { return LevelOf{d.points, d.points_magic}; }
+
 // Computes sample s of a head-row (locations lp, weights wp) and stores its
 // four corner rows (-1 = outside the level, or no sample) and w_k * a in the
 // caller's shared slots. Returns whether the sample has a corner inside its
@@ -340,14 +352,14 @@ struct Chunk {
 // sample (the caller zeroes it), for the gradient formulas; when wh is given
 // too, the level's (W, H) as floats.
 template <typename T>
-__device__ __forceinline__ bool stage_sample(const Level* levels, int points, int samples, bool live, int s,
+__device__ __forceinline__ bool stage_sample(const Level* levels, LevelOf level, int samples, bool live, int s,
                                              const T* lp, const T* wp, int4* row_slot, float4* wa_slot,
                                              float4* geo = nullptr, float2* wh = nullptr) {
   int4 r = make_int4(-1, -1, -1, -1);
   float4 wa = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   bool valid = false;
   if (live && s < samples) {
-    const Level lv = levels[s / points];
+    const Level lv = levels[level(s)];
     const float2 xy = load_loc(lp + 2 * s);
     const float a = to_f32(wp[s]);
     Corners c;

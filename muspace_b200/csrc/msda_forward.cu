@@ -99,7 +99,7 @@ __device__ __forceinline__ void substitute_outside_corners(int4* row, float4* wa
 // kSubst: the staged corners outside their level are substituted
 // (substitute_outside_corners) and every corner is loaded.
 template <typename T, int G, int kBytes, int kChunk = MSDA_FWD_CHUNK, bool kSubst = false>
-__device__ __forceinline__ void gather_head_row(const Level* levels, int points, int samples, bool live,
+__device__ __forceinline__ void gather_head_row(const Level* levels, LevelOf level, int samples, bool live,
                                                 const T* vbase, int row_stride, const T* lp, const T* wp, int sub,
                                                 int4* row, float4* wa, float2 (&acc)[Slice<T, kBytes>::kPairs]) {
   using S = Slice<T, kBytes>;
@@ -110,7 +110,7 @@ __device__ __forceinline__ void gather_head_row(const Level* levels, int points,
   for (int s0 = 0; s0 < samples; s0 += C) {
 #pragma unroll
     for (int i = sub; i < C; i += G) {
-      stage_sample(levels, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
+      stage_sample(levels, level, samples, live, s0 + i, lp, wp, row + i, wa + i);
       if constexpr (kSubst) substitute_outside_corners(row + i, wa + i);
     }
     __syncwarp();
@@ -186,12 +186,12 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_FWD_MINBLOCKS) forward_vec_k
     // 0.190 -> 0.198 ms)
     bool exact = !(MSDA_FWD_SUBST && sizeof(T) == 2) || d.spatial_size == 0;
     if (!exact) {
-      gather_head_row<T, G, kBytes, kChunk, true>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub,
+      gather_head_row<T, G, kBytes, kChunk, true>(levels, level_of(d), samples, live, vbase, row_stride, lp, wp, sub,
                                                   s_row + base, s_wa + base, acc);
       exact = __any_sync(0xffffffffu, live && !finite_pairs(acc));  // warp-uniform, rare
     }
     if (exact)
-      gather_head_row<T, G, kBytes, kChunk>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub,
+      gather_head_row<T, G, kBytes, kChunk>(levels, level_of(d), samples, live, vbase, row_stride, lp, wp, sub,
                                             s_row + base, s_wa + base, acc);
     if (live) store_slice<T, kBytes>(out + item * d.channels + sub * kCh, acc);
   }
@@ -242,12 +242,12 @@ __global__ void __launch_bounds__(kCtaThreads) scatter_div_vec_kernel(
     // substituted out-of-level corners as in forward_vec_kernel (bf16 only)
     bool exact = !(MSDA_FWD_SUBST && sizeof(T) == 2) || d.spatial_size == 0;
     if (!exact) {
-      gather_head_row<T, G, 16, MSDA_FWD_CHUNK, true>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub,
+      gather_head_row<T, G, 16, MSDA_FWD_CHUNK, true>(levels, level_of(d), samples, live, vbase, row_stride, lp, wp, sub,
                                                       s_row + base, s_wa + base, acc);
       exact = __any_sync(0xffffffffu, live && !finite_pairs(acc));
     }
     if (exact)
-      gather_head_row<T, G, 16>(levels, d.points, samples, live, vbase, row_stride, lp, wp, sub, s_row + base,
+      gather_head_row<T, G, 16>(levels, level_of(d), samples, live, vbase, row_stride, lp, wp, sub, s_row + base,
                                 s_wa + base, acc);
     const int64_t bev = index[q];
     if (live && bev >= 0 && bev < sd.num_query) {

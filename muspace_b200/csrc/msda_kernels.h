@@ -8,7 +8,18 @@ namespace msda {
 
 struct Dims {
   int batch, spatial_size, heads, channels, levels, queries, points;
+  // ceil(2^32 / points) when levels * points^2 < 2^32 and points > 1: then the
+  // level of sample s (0 <= s < levels * points) is __umulhi(s, points_magic)
+  // exactly; 0 means divide (LevelOf in msda_device.cuh)
+  uint32_t points_magic;
 };
+// The multiply-high constant of Dims::points_magic (0 when it would not be exact).
+inline uint32_t points_magic(int levels, int points) {
+  if (points <= 1 || levels <= 0) return 0;
+  const uint64_t p = static_cast<uint64_t>(points);
+  if (static_cast<uint64_t>(levels) * p * p >= (uint64_t{1} << 32)) return 0;
+  return static_cast<uint32_t>(((uint64_t{1} << 32) + p - 1) / p);
+}
 
 // One level of the level table, staged in shared memory by every CTA.
 struct Level {

@@ -178,7 +178,7 @@ __device__ __forceinline__ void issue_stage_copies(const CUtensorMap* map, const
 // in-level corner of the same sample, else the level's first pixel (pixel 0
 // past the last level), with weight 0, so all four can be loaded.
 template <bool kSubst>
-__device__ __forceinline__ void stage_staged_sample(const Level* levels, const int* stage_row, int points, int samples,
+__device__ __forceinline__ void stage_staged_sample(const Level* levels, const int* stage_row, LevelOf level, int samples,
                                                     bool live, int s, const bf16* lp, const bf16* wp, int4* row_slot,
                                                     float4* wa_slot) {
   int r[4] = {-1, -1, -1, -1};
@@ -186,7 +186,7 @@ __device__ __forceinline__ void stage_staged_sample(const Level* levels, const i
   int first = 0, shift = 0;
   bool staged = false;
   if (s < samples) {
-    const int l = s / points;
+    const int l = level(s);
     const Level lv = levels[l];
     const int sr = stage_row[l];
     first = lv.start;
@@ -230,26 +230,26 @@ __device__ __forceinline__ Words<4> lds_words(const unsigned char* p) {
 // of the warp calls it (it syncs the warp).
 template <bool kSubst>
 __device__ __forceinline__ void gather_staged_row(const Level* levels, const int* stage_row, int num_levels,
-                                                  int points, int samples, bool live, const bf16* vbase,
+                                                  LevelOf level, int samples, bool live, const bf16* vbase,
                                                   int row_stride, const unsigned char* lane_stage, uint32_t bar,
                                                   int& wait_state, const bf16* lp, const bf16* wp, int sub, int4* row,
                                                   float4* wa, float2 (&acc)[4]) {
   using S = Slice<bf16, 16>;
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
-  int lvl = 0, lvl_end = points;
+  int lvl = 0, lvl_end = level.points;
   int cur_sr = stage_row[0];
   int cur_shift = cur_sr - levels[0].start;
   for (int s0 = 0; s0 < samples; s0 += kStChunk) {
 #pragma unroll
     for (int i = sub; i < kStChunk; i += kStLanes)
-      stage_staged_sample<kSubst>(levels, stage_row, points, samples, live, s0 + i, lp, wp, row + i, wa + i);
+      stage_staged_sample<kSubst>(levels, stage_row, level, samples, live, s0 + i, lp, wp, row + i, wa + i);
     __syncwarp();
     for (int i = 0; i < kStChunk; ++i) {
       const int s = s0 + i;
       if (s >= lvl_end && lvl + 1 < num_levels) {  // warp-uniform: every group is at sample s
         ++lvl;
-        lvl_end += points;
+        lvl_end += level.points;
         cur_sr = stage_row[lvl];
         cur_shift = cur_sr - levels[lvl].start;
       }
@@ -332,10 +332,10 @@ __global__ void __launch_bounds__(kStThreads, 1)
     const bf16* lp = loc + item * samples * 2;
     const bf16* wp = weight + item * samples;
     float2 acc[4];
-    gather_staged_row<true>(levels, stage_row, d.levels, d.points, samples, live, vbase, row_stride, lane_stage, bar,
+    gather_staged_row<true>(levels, stage_row, d.levels, level_of(d), samples, live, vbase, row_stride, lane_stage, bar,
                             wait_state, lp, wp, sub, row, wa, acc);
     if (__any_sync(0xffffffffu, live && !finite_pairs(acc)))  // warp-uniform, rare
-      gather_staged_row<false>(levels, stage_row, d.levels, d.points, samples, live, vbase, row_stride, lane_stage,
+      gather_staged_row<false>(levels, stage_row, d.levels, level_of(d), samples, live, vbase, row_stride, lane_stage,
                                bar, wait_state, lp, wp, sub, row, wa, acc);
     if (live) store_slice<bf16, 16>(out + item * 32 + sub * 8, acc);
   }
