@@ -129,9 +129,16 @@ __device__ __forceinline__ int land_pairs(const Dims& d, const float* proj_b, co
 // point; or level-major): four corner rows in the (cams * S) plane of the batch entry (-1 =
 // outside the level), bilinear weights times attention, and (du, dv, weight,
 // entry) for the gradients.
+// floor(x / div): a multiply-high by magic = ceil(2^32 / div) when the caller
+// set one (exact for its range of x), else a division.
+__device__ __forceinline__ int div_by(int x, int div, uint32_t magic) {
+  return magic ? static_cast<int>(__umulhi(static_cast<uint32_t>(x), magic)) : x / div;
+}
+
+// level_magic: ceil(2^32 / per_level) for the level-major order, or 0.
 template <int G, bool kLevelMajor = false>
 __device__ __forceinline__ void stage(const Dims& d, const Map* maps, const float* off_item, const float* w_item,
-                                      int s, int samples, int slot, GroupSmem<G>& sm) {
+                                      int s, int samples, int slot, GroupSmem<G>& sm, uint32_t level_magic = 0) {
   int4 r = make_int4(-1, -1, -1, -1);
   float4 wa = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   float4 geo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -139,15 +146,15 @@ __device__ __forceinline__ void stage(const Dims& d, const Map* maps, const floa
     int pi, level, point;
     if (kLevelMajor) {  // level, then pair, then point: one level's samples of every height together
       const int per_level = samples / d.levels;  // landing pairs * points
-      level = s / per_level;
+      level = div_by(s, per_level, level_magic);
       const int rem = s - level * per_level;
-      pi = rem / d.points;
+      pi = div_by(rem, d.points, d.points_magic);
       point = rem - pi * d.points;
     } else {
       const int lp = d.levels * d.points;
-      pi = s / lp;
+      pi = div_by(s, lp, d.lp_magic);
       const int rem = s - pi * lp;
-      level = rem / d.points;
+      level = div_by(rem, d.points, d.points_magic);
       point = rem - level * d.points;
     }
     const int pr = sm.pair[pi];
@@ -389,6 +396,10 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
     const int n = land_pairs<G>(d, proj + b * d.cams * 12, c, eps, img_h, img_w, live, sub, sm, visible);
     const int samples = n * d.levels * d.points;
     const int trips = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(samples)));  // see forward
+    // the level of a sample in level-major order by a multiply-high (one division per item)
+    const int per_level = n * d.points;
+    const uint32_t level_magic =
+        per_level > 1 && static_cast<uint64_t>(samples) * per_level < (uint64_t{1} << 32) ? 0xffffffffu / per_level + 1 : 0;
     const int64_t plane = b * d.cams * static_cast<int64_t>(d.stride_n) * d.channels + head * per_head + sub * 4;
     const float* vb = value + plane;
     float* gvb = grad_value + plane;
@@ -403,7 +414,7 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
     for (int s0 = 0; s0 < trips; s0 += Cs) {
       if (sub % Sh::kBwdStager == 0) {
         const int i = sub / Sh::kBwdStager;
-        stage<G, true>(d, maps, off_item, w_item, s0 + i, samples, i, sm);
+        stage<G, true>(d, maps, off_item, w_item, s0 + i, samples, i, sm, level_magic);
       }
       __syncwarp();
       // samples of one level around the heights of a camera share corner rows

@@ -21,6 +21,10 @@ namespace fsca {
 struct Dims {
   int batch, cams, stride_n, channels, levels, heads, points;
   int gx, gy, gz;
+  // ceil(2^32 / d) for d = points and d = levels * points, set by the host
+  // where a multiply-high by it equals the division for every sample index the
+  // kernels divide (kMaxPairs pairs of levels * points samples); 0: divide
+  uint32_t points_magic, lp_magic;
 };
 
 // Voxel grid: centre of cell (ix, iy, iz) = min + (i + 0.5) * size. The

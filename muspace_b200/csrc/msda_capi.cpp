@@ -705,8 +705,18 @@ FscaViews fsca_views(const DLTensor* value, const DLTensor* proj, const DLTensor
   const int64_t kMax = std::numeric_limits<int32_t>::max();
   require(cams * stride <= kMax && batch * gx * gy <= kMax && channels <= kMax, "a size exceeds the supported range");
   FscaViews v{};
+  // floor(x / d) == umulhi(x, ceil(2^32 / d)) whenever x * d < 2^32; the kernels divide sample
+  // indices below kMaxPairs * L * P by P and by L * P, and within one (cell, head) indices below
+  // that many by P
+  const auto magic = [](uint64_t d, uint64_t x_max) -> uint32_t {
+    if (d <= 1 || x_max * d >= (uint64_t{1} << 32)) return 0;
+    return static_cast<uint32_t>(((uint64_t{1} << 32) + d - 1) / d);
+  };
+  const uint64_t lp = static_cast<uint64_t>(levels) * static_cast<uint64_t>(points);
   v.dims = fsca::Dims{static_cast<int>(batch), static_cast<int>(cams), static_cast<int>(stride),
-                      static_cast<int>(channels), static_cast<int>(levels), heads, points, gx, gy, gz};
+                      static_cast<int>(channels), static_cast<int>(levels), heads, points, gx, gy, gz,
+                      magic(static_cast<uint64_t>(points), fsca::kMaxPairs * lp),
+                      magic(lp, fsca::kMaxPairs * lp)};
   v.args.value = static_cast<const float*>(data_of(value));
   v.args.projection = static_cast<const float*>(data_of(proj));
   v.args.shapes = static_cast<const int*>(data_of(spatial));
