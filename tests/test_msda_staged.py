@@ -137,7 +137,7 @@ def test_the_variable_selects_the_staged_kernel(cuda_device):
     inp = _inputs(cuda_device, "detr", seed=9)
     launched = {}
     for staged in (False, True):
-        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA], acc_events=True) as prof:
             _forward(inp, staged=staged)
             torch.cuda.synchronize()
         launched[staged] = " ".join(e.name for e in prof.events())
