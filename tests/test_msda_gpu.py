@@ -135,13 +135,15 @@ def _random_case(channels, levels, points, seed, batch=2, queries=7, heads=2):
 
 
 @pytest.mark.parametrize("channels", [4, 8, 16, 32, 128, 256])
-@pytest.mark.parametrize("levels,points", [(3, 3), (1, 1), (4, 2)])
+@pytest.mark.parametrize("levels,points", [(3, 3), (1, 1), (4, 2), (2, 7), (4, 13)])
 def test_every_lane_layout_matches_c_oracle(cuda_device, channels, levels, points):
     """Head-rows of 4..256 channels take every lane layout of the vector
     kernels (1 to 32 lanes of 8 or 16 bytes, the lane-pair backward for bf16
     D = 16 / 32 with more than 4 samples, and the scalar kernels for fp32
-    D = 256); 1, 8 and 9 samples per head-row cover a chunk of staged samples
-    that is partly empty, exactly full, or followed by a short one."""
+    D = 256); 1, 8, 9, 14 and 52 samples per head-row cover a chunk of staged
+    samples that is partly empty, exactly full, or followed by a short one, and
+    point counts that are not powers of two (the level of a sample comes from
+    a multiply-high by a host constant, not a division)."""
     g = _random_case(channels, levels, points, seed=channels * 100 + levels * 10 + points)
     for dtype, tol in ((torch.float32, FP32_TOL), (torch.bfloat16, BF16_TOL)):
         q = {k: (torch.from_numpy(v).to(dtype).float().numpy() if v.dtype == np.float32 else v) for k, v in g.items()}
