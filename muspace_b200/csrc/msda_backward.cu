@@ -21,8 +21,8 @@
 // corner's whole 128-byte fp32 grad_value line). The head-row's samples are
 // taken in chunks of Cs = min(G, 8) (4 for head-rows of at most 4 samples):
 //  1. stage: the lane at sub = i * G / Cs computes the geometry of chunk
-//     sample i once and stages its four corner rows, w_k * a and (lh, lw, a)
-//     in shared memory;
+//     sample i once and stages its four corner rows, w_k * a and
+//     (lh, lw, W a, H a) in shared memory;
 //  2. fold: the chunk's 4 Cs (corner row, w_k * a) entries are merged by row
 //     (samples of one head-row cluster, so at coarse levels most corners
 //     repeat: on BEVFormer-like locations 117 corner rows per head-row shrink
@@ -32,10 +32,12 @@
 //     FMAs) and sends (sum of w_k * a) * g for each first-occurrence row with
 //     red.global.add.v4.f32; after every round of Cd samples (4 for bf16, 2
 //     for fp32) a transpose reduction hands one lane per sample the four T_k,
-//     from which it writes
+//     which it puts in shared memory;
+//  4. after the rounds every stager lane writes its own sample's
 //       grad_w = sum_k w_k T_k,
 //       grad_x = W a (hh (T_1 - T_0) + lh (T_3 - T_2)),
-//       grad_y = H a (hw (T_2 - T_0) + lw (T_3 - T_1)).
+//       grad_y = H a (hw (T_2 - T_0) + lw (T_3 - T_1))
+//     (the whole chunk in one pass of the warp, contiguous stores).
 // That is backward_vec_kernel. For bf16 D = 16 / 32 (every BEVFormer shape)
 // backward_pair_kernel runs instead: the
 // same stage and fold, then a lane pair forms one sample's dots (no transpose
@@ -233,10 +235,12 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
 //  - dots: a lane pair owns a sample, lane h of the pair holding chunks h,
 //    h + 2, ... (so the pair's first loads fill whole 32-byte sectors); it
 //    gathers those chunks of the four corners, forms the corner dots with its
-//    grad_output chunks, one xor shuffle completes them, and lane 0 of the pair
-//    writes grad_w / grad_loc: no transpose reduction, no geometry per lane;
+//    grad_output chunks, xor shuffles complete them, and lane 0 of the pair
+//    (or quad, kLPS = 4) puts them in shared memory: no transpose reduction;
 //  - REDs: every lane sends its 4-channel slice of (sum of w_k a) * g for each
-//    first-occurrence corner row (whole 128-byte lines per group for D = 32).
+//    first-occurrence corner row (whole 128-byte lines per group for D = 32);
+//  - grad_w / grad_loc as in backward_vec_kernel, once per chunk by the stager
+//    lanes.
 
 // CTAs per SM the lane-pair kernel's register budget is sized for (4: 64
 // registers, 32 resident warps; 8.60 -> 8.06 ms for the c4 backward against 3).
