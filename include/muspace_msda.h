@@ -174,7 +174,7 @@ MSDA_API int msda_backward(msda_dtype_t dtype, const msda_dims_t *dims, const vo
  *
  * Cost: the bucketed backward is slower than the fused backward that
  * msda_backward runs by default (measured on B200, bf16, BEVFormer SCA shapes:
- * 2.52 ms against 1.06 ms for 6 camera images, 0.92 against 0.39 ms for 2).
+ * 2.41 ms against 0.94 ms for 6 camera images, 0.87 against 0.34 ms for 2).
  * msda_backward itself allocates nothing either in a default build (its fused
  * kernels need no work space); only builds with -DMSDA_BUCKETED_BACKWARD=1
  * make it take the bucket plan from the stream-ordered allocator. Callers that
