@@ -71,6 +71,8 @@ def parse_args():
     p.add_argument("--per-image", action="store_true",
                    help="--variant query: backward and grad_value reduce-scatter per camera image, overlapped")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    p.add_argument("--e2e-streams", type=int, default=1,
+                   help="copy streams per direction in the end-to-end leg (a tensor always on the same one)")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-other-workloads", action="store_true",
                    help="skip the short device-time runs of the other configs and ops (N = 1 only)")
@@ -498,43 +500,64 @@ class E2ESlot:
         self.inputs, self.outputs, self.step = inputs, outputs, step
 
 
-def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device) -> float:
+def _spread(tensors, n: int) -> list[int]:
+    """Stream index of each tensor: largest first onto the least-loaded of n."""
+    load = [0] * n
+    where = [0] * len(tensors)
+    for k in sorted(range(len(tensors)), key=lambda k: -tensors[k].numel() * tensors[k].element_size()):
+        w = min(range(n), key=lambda x: load[x])
+        where[k] = w
+        load[w] += tensors[k].numel() * tensors[k].element_size()
+    return where
+
+
+def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device, copy_streams: int = 1) -> float:
     """Device time per step of ``steps`` end-to-end steps, each with the H2D
     copy of its inputs from pinned host memory and the D2H copy of all its
-    outputs, double-buffered over ``slots`` (two sets of device buffers) on
-    three streams: the H2D of step i + 1 and the D2H of step i - 1 overlap the
-    compute of step i, and the two copy directions run concurrently (PCIe is
-    full duplex). A slot's inputs are rewritten only after its previous
-    compute, and its outputs only after their previous D2H. Max over ranks."""
+    outputs, double-buffered over ``slots`` (two sets of device buffers): the
+    H2D of step i + 1 and the D2H of step i - 1 overlap the compute of step i,
+    and the two copy directions run concurrently (PCIe is full duplex). Each
+    direction's copies are spread over ``copy_streams`` streams (a tensor
+    always on the same one). A slot's inputs are rewritten only after its
+    previous compute, and its outputs only after their previous D2H. Max over
+    ranks."""
     import torch.distributed as dist
 
-    s_in, s_comp, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device), torch.cuda.Stream(device)
-    # one pinned output set: the D2H copies of the slots run one after another
-    # on s_out, so they never write it at the same time (and a rank pins its
-    # inputs and outputs once, not twice, which matters with 8 ranks a node)
+    s_comp = torch.cuda.Stream(device)
+    s_in = [torch.cuda.Stream(device) for _ in range(copy_streams)]
+    s_out = [torch.cuda.Stream(device) for _ in range(copy_streams)]
+    # one pinned output set: a tensor's D2H copies of the slots run one after
+    # another on its stream, so they never write it at the same time (and a
+    # rank pins its inputs and outputs once, not twice, which matters with 8
+    # ranks a node)
     host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in slots[0].outputs]
-    in_done = [torch.cuda.Event() for _ in slots]
+    in_where, out_where = _spread(host_in, copy_streams), _spread(host_out, copy_streams)
+    in_done = [[torch.cuda.Event() for _ in s_in] for _ in slots]
     comp_done = [torch.cuda.Event() for _ in slots]
-    out_done = [torch.cuda.Event() for _ in slots]
+    out_done = [[torch.cuda.Event() for _ in s_out] for _ in slots]
 
     def one(i):
         j = i % len(slots)
         slot = slots[j]
-        s_in.wait_event(comp_done[j])
-        with torch.cuda.stream(s_in):
-            for dst, src in zip(slot.inputs, host_in):
-                dst.copy_(src, non_blocking=True)
-        in_done[j].record(s_in)
-        s_comp.wait_event(in_done[j])
-        s_comp.wait_event(out_done[j])
+        for k, s in enumerate(s_in):
+            s.wait_event(comp_done[j])
+            with torch.cuda.stream(s):
+                for dst, src, w in zip(slot.inputs, host_in, in_where):
+                    if w == k:
+                        dst.copy_(src, non_blocking=True)
+            in_done[j][k].record(s)
+        for e in in_done[j] + out_done[j]:
+            s_comp.wait_event(e)
         with torch.cuda.stream(s_comp):
             slot.step()
         comp_done[j].record(s_comp)
-        s_out.wait_event(comp_done[j])
-        with torch.cuda.stream(s_out):
-            for dst, src in zip(host_out, slot.outputs):
-                dst.copy_(src, non_blocking=True)
-        out_done[j].record(s_out)
+        for k, s in enumerate(s_out):
+            s.wait_event(comp_done[j])
+            with torch.cuda.stream(s):
+                for dst, src, w in zip(host_out, slot.outputs, out_where):
+                    if w == k:
+                        dst.copy_(src, non_blocking=True)
+            out_done[j][k].record(s)
 
     for i in range(len(slots)):  # warm-up: every slot once
         one(i)
@@ -542,11 +565,13 @@ def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device) -> floa
     if distributed:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(s_in)
+    start.record(s_in[0])
+    for s in s_in[1:] + [s_comp] + s_out:
+        s.wait_event(start)
     for i in range(steps):
         one(i)
     main = torch.cuda.current_stream(device)
-    for s in (s_in, s_comp, s_out):
+    for s in s_in + [s_comp] + s_out:
         main.wait_stream(s)
     end.record(main)
     torch.cuda.synchronize(device)
@@ -557,7 +582,7 @@ def pipelined_e2e(slots, host_in, steps: int, distributed: bool, device) -> floa
 
 
 E2E_PATH = ("pinned host buffers -> cudaMemcpyAsync H2D -> {calls} (C-ABI) -> cudaMemcpyAsync D2H -> pinned host; "
-            "two device buffer sets, H2D / compute / D2H on three streams")
+            "two device buffer sets, compute on one stream, H2D and D2H on {streams} stream(s) each")
 
 
 def run_e2e(args, local, dtype, inp, device, job_total, distributed):
@@ -571,7 +596,7 @@ def run_e2e(args, local, dtype, inp, device, job_total, distributed):
         step = Step(dev_in, dtype, device)
         slots.append(E2ESlot([dev_in[k] for k in keys], [step.out, step.gv, step.gl, step.gw], step))
     steps = max(3, min(args.steps, 10))
-    ms = pipelined_e2e(slots, host_in, steps, distributed, device)
+    ms = pipelined_e2e(slots, host_in, steps, distributed, device, args.e2e_streams)
     return {
         "value": round(job_total / (ms / 1e3) / 1e9, 3),
         "unit": "GB/s",
@@ -579,7 +604,7 @@ def run_e2e(args, local, dtype, inp, device, job_total, distributed):
         "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in slots[0].outputs),
         "ms_per_step": round(ms, 3),
         "steps": steps,
-        "path": E2E_PATH.format(calls="ms_deform_attn_forward/backward"),
+        "path": E2E_PATH.format(calls="ms_deform_attn_forward/backward", streams=args.e2e_streams),
     }
 
 
@@ -840,11 +865,11 @@ def run_op(args, rank, world, device):
         second = OpWorkload(args.op, device)  # the second device buffer set of the pipeline
         slots = [E2ESlot(x.inputs, x.outputs, x.step) for x in (w, second)]
         steps = max(3, min(args.steps, 10))
-        e2e_ms = pipelined_e2e(slots, host_in, steps, world > 1, device)
+        e2e_ms = pipelined_e2e(slots, host_in, steps, world > 1, device, args.e2e_streams)
         e2e = {"value": round(w.bytes * world / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": _nbytes(*host_in), "d2h_bytes_per_step": _nbytes(*w.outputs),
                "ms_per_step": round(e2e_ms, 3), "steps": steps,
-               "path": E2E_PATH.format(calls=w.calls)}
+               "path": E2E_PATH.format(calls=w.calls, streams=args.e2e_streams)}
         del second, slots
     if rank != 0:
         return None
