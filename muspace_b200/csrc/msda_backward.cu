@@ -80,6 +80,13 @@ namespace msda {
 #ifndef MSDA_BWD_QUAD
 #define MSDA_BWD_QUAD 1
 #endif
+// 1: for head-rows of at most 4 samples with one 16-byte chunk per lane (all
+// four corners in flight) the first dot pass's gathers are issued before the
+// row fold (c3 backward 0.275 -> 0.262 ms, bevformer-1l bf16 0.269 -> 0.262;
+// with four passes per chunk, as at c4, it measured 0.5-1 % slower).
+#ifndef MSDA_BWD_PREFETCH
+#define MSDA_BWD_PREFETCH 1
+#endif
 // 1: the lane-pair kernel also takes bf16 head-rows of at most 4 samples.
 #ifndef MSDA_PAIR_SHORT
 #define MSDA_PAIR_SHORT 1
@@ -332,61 +339,8 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
             valid ? make_float4(geo.x, geo.y, wh.x * geo.z, wh.y * geo.z) : make_float4(-1.0f, 0.0f, 0.0f, 0.0f);
       }
       __syncwarp();
-#if MSDA_BWD_DEDUP
-      if constexpr (kScatter) {
-#if MSDA_BWD_HASH_FOLD
-        fold_rows_hashed<G, 4 * Cs, kHashSlots>(reinterpret_cast<const int*>(s_row + base),
-                                                reinterpret_cast<float*>(s_wa + base),
-                                                s_hash + (threadIdx.x / G) * kHashSlots, sub);
-#else
-        fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(s_row + base),
-                                      reinterpret_cast<float*>(s_wa + base), sub);
-#endif
-      }
-#endif
-#pragma unroll 1
-      for (int p = 0; p < kPasses; ++p) {
-        // dots of sample i by the pair
-        const int i = p * kPerPass + member;
-        if (i < Cs) {
-          const int4 r4 = s_row[base + i];
-          const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
-          float t[4];
-#pragma unroll
-          for (int k0 = 0; k0 < 4; k0 += Sh::kCornersInFlight) {
-            Words<4> raw[Sh::kCornersInFlight][kCPL];
-#pragma unroll
-            for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
-              const int row = rows[k0 + kk];
-#pragma unroll
-              for (int j = 0; j < kCPL; ++j)
-                raw[kk][j] = row >= 0 ? ldg_words<16>(vrow + static_cast<int64_t>(row) * row_stride +
-                                                      (j * kLPS + lq) * Sh::kPer16)
-                                      : zero_words<4>();
-            }
-#pragma unroll
-            for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
-              float2 acc = make_float2(0.0f, 0.0f);
-#pragma unroll
-              for (int j = 0; j < kCPL; ++j) {
-                if constexpr (kMixed) {
-#pragma unroll
-                  for (int q = 0; q < 4; ++q) acc = fma_bf16x2_f32(graw[j].w[q], raw[kk][j].w[q], acc);
-                } else {
-#pragma unroll
-                  for (int q = 0; q < Sh::kPairs16; ++q) acc = ffma2(ga[j][q], S16::pair(raw[kk][j], q), acc);
-                }
-              }
-              t[k0 + kk] = acc.x + acc.y;
-            }
-          }
-#pragma unroll
-          for (int m = 1; m < kLPS; m <<= 1)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], m);
-          if (lq == 0) s_dots[base + i] = make_float4(t[0], t[1], t[2], t[3]);
-        }
-        // REDs of the same samples by every lane's slice
+      // REDs of pass p's samples by every lane's slice
+      auto pass_reds = [&](int p) {
         if constexpr (kScatter) {
 #pragma unroll
           for (int m = 0; m < kPerPass; ++m) {
@@ -410,6 +364,122 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
 #endif
             }
           }
+        }
+      };
+      if constexpr (kCPL == 1 && kStageMax == 4 && MSDA_BWD_PREFETCH) {
+        // head-rows of at most 4 samples, all four corners in flight: the first
+        // of the chunk's two passes has its gathers issued before the fold, so
+        // their latency hides behind its shared-memory work
+        auto gather_corners = [&](int i, Words<4> (&raw)[4]) {
+          const int4 r4 = s_row[base + i];
+          const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            raw[k] = rows[k] >= 0 ? ldg_words<16>(vrow + static_cast<int64_t>(rows[k]) * row_stride + lq * Sh::kPer16)
+                                  : zero_words<4>();
+        };
+        auto dots = [&](int i, const Words<4> (&raw)[4]) {
+          float t[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float2 acc = make_float2(0.0f, 0.0f);
+            if constexpr (kMixed) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) acc = fma_bf16x2_f32(graw[0].w[q], raw[k].w[q], acc);
+            } else {
+#pragma unroll
+              for (int q = 0; q < Sh::kPairs16; ++q) acc = ffma2(ga[0][q], S16::pair(raw[k], q), acc);
+            }
+            t[k] = acc.x + acc.y;
+          }
+#pragma unroll
+          for (int m = 1; m < kLPS; m <<= 1)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], m);
+          if (lq == 0) s_dots[base + i] = make_float4(t[0], t[1], t[2], t[3]);
+        };
+        Words<4> first[4];
+        if (member < Cs) gather_corners(member, first);
+#if MSDA_BWD_DEDUP
+        if constexpr (kScatter) {
+#if MSDA_BWD_HASH_FOLD
+          fold_rows_hashed<G, 4 * Cs, kHashSlots>(reinterpret_cast<const int*>(s_row + base),
+                                                  reinterpret_cast<float*>(s_wa + base),
+                                                  s_hash + (threadIdx.x / G) * kHashSlots, sub);
+#else
+          fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(s_row + base),
+                                        reinterpret_cast<float*>(s_wa + base), sub);
+#endif
+        }
+#endif
+        if (member < Cs) dots(member, first);
+        pass_reds(0);
+#pragma unroll 1
+        for (int p = 1; p < kPasses; ++p) {
+          const int i = p * kPerPass + member;
+          if (i < Cs) {
+            Words<4> raw[4];
+            gather_corners(i, raw);
+            dots(i, raw);
+          }
+          pass_reds(p);
+        }
+      } else {
+#if MSDA_BWD_DEDUP
+        if constexpr (kScatter) {
+#if MSDA_BWD_HASH_FOLD
+          fold_rows_hashed<G, 4 * Cs, kHashSlots>(reinterpret_cast<const int*>(s_row + base),
+                                                  reinterpret_cast<float*>(s_wa + base),
+                                                  s_hash + (threadIdx.x / G) * kHashSlots, sub);
+#else
+          fold_repeated_rows<G, 4 * Cs>(reinterpret_cast<const int*>(s_row + base),
+                                        reinterpret_cast<float*>(s_wa + base), sub);
+#endif
+        }
+#endif
+#pragma unroll 1
+        for (int p = 0; p < kPasses; ++p) {
+          // dots of sample i by the pair
+          const int i = p * kPerPass + member;
+          if (i < Cs) {
+            const int4 r4 = s_row[base + i];
+            const int rows[4] = {r4.x, r4.y, r4.z, r4.w};
+            float t[4];
+#pragma unroll
+            for (int k0 = 0; k0 < 4; k0 += Sh::kCornersInFlight) {
+              Words<4> raw[Sh::kCornersInFlight][kCPL];
+#pragma unroll
+              for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
+                const int row = rows[k0 + kk];
+#pragma unroll
+                for (int j = 0; j < kCPL; ++j)
+                  raw[kk][j] = row >= 0 ? ldg_words<16>(vrow + static_cast<int64_t>(row) * row_stride +
+                                                        (j * kLPS + lq) * Sh::kPer16)
+                                        : zero_words<4>();
+              }
+#pragma unroll
+              for (int kk = 0; kk < Sh::kCornersInFlight; ++kk) {
+                float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int j = 0; j < kCPL; ++j) {
+                  if constexpr (kMixed) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc = fma_bf16x2_f32(graw[j].w[q], raw[kk][j].w[q], acc);
+                  } else {
+#pragma unroll
+                    for (int q = 0; q < Sh::kPairs16; ++q) acc = ffma2(ga[j][q], S16::pair(raw[kk][j], q), acc);
+                  }
+                }
+                t[k0 + kk] = acc.x + acc.y;
+              }
+            }
+#pragma unroll
+            for (int m = 1; m < kLPS; m <<= 1)
+#pragma unroll
+              for (int k = 0; k < 4; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], m);
+            if (lq == 0) s_dots[base + i] = make_float4(t[0], t[1], t[2], t[3]);
+          }
+          pass_reds(p);
         }
       }
       __syncwarp();
