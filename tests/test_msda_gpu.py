@@ -428,3 +428,24 @@ def test_non_finite_values_next_to_out_of_level_corners(cuda_device, dtype):
     tol = FP32_TOL if dtype == torch.float32 else BF16_TOL
     fin = torch.isfinite(expected)
     torch.testing.assert_close(got[fin], expected[fin], rtol=tol, atol=tol)
+
+
+def test_value_beyond_2_31_elements_indexes_every_image(cuda_device):
+    """c2 shapes at 320 images (Lq 2000; a multiple of the im2col step): `value`
+    holds 2.5e9 elements, so image 272 straddles 2^31 elements and image 319
+    lies wholly past it, where a 32-bit offset anywhere in the kernels would
+    read or write the wrong image. The batched call must equal each image run
+    alone (forward, grad_loc and grad_w bit for bit; grad_value up to the order
+    of its fp32 reductions)."""
+    cfg = cases.CONFIGS["c2"].with_(batch=320, queries=2000)
+    inp = cases.make_inputs(cfg, dtype=torch.bfloat16, device=cuda_device)
+    assert inp["value"].numel() > 2**31
+    out, (gv, gl, gw) = _c_abi_fwd_bwd(inp, torch.bfloat16)
+    for b in (0, 272, 319):
+        part = {k: (v[b : b + 1].contiguous() if k not in ("spatial_shapes", "level_start_index") else v)
+                for k, v in inp.items()}
+        o, (pgv, pgl, pgw) = _c_abi_fwd_bwd(part, torch.bfloat16)
+        assert torch.equal(o, out[b : b + 1])
+        assert torch.equal(pgl, gl[b : b + 1])
+        assert torch.equal(pgw, gw[b : b + 1])
+        torch.testing.assert_close(pgv, gv[b : b + 1], rtol=1e-5, atol=1e-5)
