@@ -66,23 +66,40 @@ __device__ __forceinline__ FixedPoint fixed_point(const unsigned* header, int he
 }
 
 // Step 2: one warp per head-row (b, q, h). Lane i computes the geometry of
-// sample s0 + i once; the warp then walks the samples, broadcasting each
-// one's corner rows and w_k * a, with lanes over the channels.
+// sample s0 + i once; the pass's corner entries (4 per sample) go to shared
+// memory, repeated corner rows are chained to their first claimer through a
+// per-warp hash table, and the warp then walks the claimers with lanes over
+// the channels: each lane converts every contribution of a claimer's chain
+// to fixed point exactly as it would alone, sums them in a register (integer
+// sums are exact, so the result is the same bits as one atomic per entry)
+// and issues one atomic per distinct row.
+constexpr int kDetWarps = 8;             // 256 threads
+constexpr int kDetEntries = 4 * 32;      // corner entries of one 32-sample pass
+constexpr int kDetTable = 2 * kDetEntries;
+
 template <typename T>
 __global__ void __launch_bounds__(256) fixed_point_scatter_kernel(
     Dims d, const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts, const T* __restrict__ loc,
     const T* __restrict__ weight, const T* __restrict__ grad_out, const unsigned* __restrict__ header,
     int headroom_bits, unsigned long long* __restrict__ acc, float* __restrict__ grad_value) {
   extern __shared__ Level levels[];
+  __shared__ int s_table[kDetWarps][kDetTable];
+  __shared__ int s_row[kDetWarps][kDetEntries];
+  __shared__ float s_wa[kDetWarps][kDetEntries];
+  __shared__ int s_next[kDetWarps][kDetEntries];  // claimer: chain head; repeat: next repeat (-1 ends)
   stage_levels(levels, shapes, starts, d);
   const FixedPoint fp = fixed_point(header, headroom_bits);
-  const int lane = threadIdx.x % 32;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  int* table = s_table[warp];
+  int* erow = s_row[warp];
+  float* ewa = s_wa[warp];
+  int* enext = s_next[warp];
   const int64_t items = static_cast<int64_t>(d.batch) * d.queries * d.heads;
   const int64_t row_stride = static_cast<int64_t>(d.heads) * d.channels;
   const int samples = d.levels * d.points;
+  const LevelOf level = level_of(d);
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32; item < items;
-       item += warps) {
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp; item < items; item += warps) {
     const int h = static_cast<int>(item % d.heads);
     const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
     const int64_t head0 = b * d.spatial_size * row_stride + static_cast<int64_t>(h) * d.channels;
@@ -94,7 +111,7 @@ __global__ void __launch_bounds__(256) fixed_point_scatter_kernel(
         const float2 xy = load_loc(loc + 2 * so);
         const float a = to_f32(weight[so]);
         Corners c;
-        if (corners(levels[(s0 + lane) / d.points], xy.x, xy.y, c)) {
+        if (corners(levels[level(s0 + lane)], xy.x, xy.y, c)) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             row[k] = c.row[k];
@@ -103,23 +120,60 @@ __global__ void __launch_bounds__(256) fixed_point_scatter_kernel(
         }
       }
       const int n = samples - s0 < 32 ? samples - s0 : 32;
+      __syncwarp();  // the previous pass has finished reading the entries
+#pragma unroll
+      for (int t = lane; t < kDetTable; t += 32) table[t] = -1;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        erow[4 * lane + k] = row[k];
+        ewa[4 * lane + k] = wa[k];
+        enext[4 * lane + k] = -1;
+      }
+      __syncwarp();
+      // claims: the first entry to take a row's slot owns the row; an entry
+      // finding its row's slot taken by another row stays on its own
+      int owner[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = 4 * lane + k;
+        owner[k] = e;
+        if (row[k] >= 0) {
+          const int slot = static_cast<int>((static_cast<uint32_t>(row[k]) * 2654435761u) >> 24);  // 256 slots
+          const int held = atomicCAS(table + slot, -1, e);
+          if (held >= 0 && erow[held] == row[k]) owner[k] = held;
+        }
+      }
+      __syncwarp();
+      // repeats join their owner's chain (owners are never repeats, so a
+      // repeat's own link is written by it alone)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = 4 * lane + k;
+        if (owner[k] != e) {
+          enext[e] = atomicExch(enext + owner[k], e);
+          erow[e] = -2;  // reached through its owner
+        }
+      }
+      __syncwarp();
       for (int c0 = 0; c0 < d.channels; c0 += 32) {
         const int ch = c0 + lane;
         const bool active = ch < d.channels;
         const float gc = active ? to_f32(grad_out[item * d.channels + ch]) : 0.0f;
-        for (int j = 0; j < n; ++j) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int r = __shfl_sync(0xffffffffu, row[k], j);
-            const float w = __shfl_sync(0xffffffffu, wa[k], j);
-            if (!active || r < 0) continue;
-            const float contribution = w * gc;
-            const int64_t at = head0 + static_cast<int64_t>(r) * row_stride + ch;
-            if (fp.finite)
-              atomicAdd(acc + at, static_cast<unsigned long long>(
-                                      __double2ll_rn(static_cast<double>(contribution) * fp.scale)));
-            else
-              atomicAdd(grad_value + at, contribution);
+        for (int e = 0; e < 4 * n; ++e) {
+          const int r = erow[e];
+          if (r < 0) continue;  // outside the level, no sample, or a repeat (warp-uniform)
+          if (fp.finite) {
+            const auto fixed = [&](float contribution) -> long long {
+              return __double2ll_rn(static_cast<double>(contribution) * fp.scale);
+            };
+            long long sum = fixed(ewa[e] * gc);
+            for (int x = enext[e]; x >= 0; x = enext[x]) sum += fixed(ewa[x] * gc);
+            if (active)
+              atomicAdd(acc + head0 + static_cast<int64_t>(r) * row_stride + ch, static_cast<unsigned long long>(sum));
+          } else {
+            float sum = ewa[e] * gc;
+            for (int x = enext[e]; x >= 0; x = enext[x]) sum += ewa[x] * gc;
+            if (active) atomicAdd(grad_value + head0 + static_cast<int64_t>(r) * row_stride + ch, sum);
           }
         }
       }
