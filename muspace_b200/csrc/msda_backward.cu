@@ -267,6 +267,9 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
   constexpr int Cs = G < kStageMax ? G : kStageMax;  // samples staged per chunk
   constexpr int kStage = G / Cs;                     // stager lanes: sub % kStage == 0
   constexpr int kPerPass = G / kLPS;                  // samples whose dots run at once
+  // every lane's sample of a pass exists (i < Cs), so the full-warp shuffles of
+  // the dots below are reached by all lanes
+  static_assert(kPerPass <= Cs && Cs % kPerPass == 0, "a pass's samples must lie inside the staged chunk");
   constexpr int kPasses = Cs / kPerPass > 0 ? Cs / kPerPass : 1;
   constexpr int kGroups = kCtaThreads / G;
   constexpr int kSlots = Cs + 1;
