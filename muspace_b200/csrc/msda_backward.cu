@@ -140,8 +140,9 @@ __global__ void __launch_bounds__(kCtaThreads, kMinBlocks<T, kBytes>) backward_v
     const bool live = item < items;
     const int64_t slot = live ? item : items - 1;
     const int64_t it = order ? order[slot] : slot;
-    const int h = static_cast<int>(it % d.heads);
-    const int64_t b = it / (static_cast<int64_t>(d.queries) * d.heads);
+    const ImageHead ih = image_head(it, d, items < (int64_t{1} << 31));
+    const int h = ih.h;
+    const int64_t b = ih.b;
     const int64_t head0 = (b * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     const T* vbase = value + head0;
     float* gbase = grad_value + head0;
@@ -295,8 +296,9 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_PAIR_MINBLOCKS) backward_pai
     const bool live = item < items;
     const int64_t slot = live ? item : items - 1;
     const int64_t it = order ? order[slot] : slot;
-    const int h = static_cast<int>(it % d.heads);
-    const int64_t b = it / (static_cast<int64_t>(d.queries) * d.heads);
+    const ImageHead ih = image_head(it, d, items < (int64_t{1} << 31));
+    const int h = ih.h;
+    const int64_t b = ih.b;
     const int64_t head0 = (b * d.spatial_size) * row_stride + h * d.channels;
     const T* vrow = value + head0;
     float* gbase = grad_value + head0 + sub * 4;

@@ -345,6 +345,22 @@ struct LevelOf {
 };
 __device__ __forceinline__ LevelOf level_of(const Dims& d) { return LevelOf{d.points, d.points_magic}; }
 
+// Image and head of head-row `item` ((b, q, h) order, heads fastest): 32-bit
+// divisions when every head-row index of the call fits 31 bits (idx32; every
+// realistic call), else the 64-bit ones.
+struct ImageHead {
+  int64_t b;
+  int h;
+};
+__device__ __forceinline__ ImageHead image_head(int64_t item, const Dims& d, bool idx32) {
+  if (idx32) {
+    const uint32_t i = static_cast<uint32_t>(item);
+    return ImageHead{static_cast<int64_t>(i / static_cast<uint32_t>(d.queries * d.heads)),
+                     static_cast<int>(i % static_cast<uint32_t>(d.heads))};
+  }
+  return ImageHead{item / (static_cast<int64_t>(d.queries) * d.heads), static_cast<int>(item % d.heads)};
+}
+
 // Computes sample s of a head-row (locations lp, weights wp) and stores its
 // four corner rows (-1 = outside the level, or no sample) and w_k * a in the
 // caller's shared slots. Returns whether the sample has a corner inside its

@@ -175,8 +175,9 @@ __global__ void __launch_bounds__(kCtaThreads, MSDA_FWD_MINBLOCKS) forward_vec_k
        slot - (threadIdx.x % 32) / G < items; slot += stride) {
     const bool live = slot < items;
     const int64_t item = order ? order[live ? slot : items - 1] : (live ? slot : items - 1);
-    const int h = static_cast<int>(item % d.heads);
-    const int64_t b = item / (static_cast<int64_t>(d.queries) * d.heads);
+    const ImageHead ih = image_head(item, d, items < (int64_t{1} << 31));
+    const int h = ih.h;
+    const int64_t b = ih.b;
     const T* vbase = value + (b * d.spatial_size) * row_stride + h * d.channels + sub * kCh;
     float2 acc[kPairs];
     const T* lp = loc + item * samples * 2;
