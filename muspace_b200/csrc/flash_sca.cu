@@ -129,6 +129,27 @@ __device__ __forceinline__ int land_pairs(const Dims& d, const float* proj_b, co
 // point; or level-major): four corner rows in the (cams * S) plane of the batch entry (-1 =
 // outside the level), bilinear weights times attention, and (du, dv, weight,
 // entry) for the gradients.
+// Head, cell (x, y) and batch entry of item (b, gy, gx, heads order): 32-bit
+// divisions when every item index of the call fits 31 bits (idx32), else
+// 64-bit ones.
+struct ItemCell {
+  int head, ix, iy;
+  int64_t cell, b;
+};
+__device__ __forceinline__ ItemCell item_cell(int64_t it, const Dims& d, bool idx32) {
+  if (idx32) {
+    const uint32_t i = static_cast<uint32_t>(it);
+    const uint32_t cell = i / static_cast<uint32_t>(d.heads);
+    const uint32_t row = cell / static_cast<uint32_t>(d.gx);
+    return ItemCell{static_cast<int>(i - cell * static_cast<uint32_t>(d.heads)),
+                    static_cast<int>(cell - row * static_cast<uint32_t>(d.gx)),
+                    static_cast<int>(row % static_cast<uint32_t>(d.gy)), cell, row / static_cast<uint32_t>(d.gy)};
+  }
+  const int64_t cell = it / d.heads;
+  return ItemCell{static_cast<int>(it % d.heads), static_cast<int>(cell % d.gx),
+                  static_cast<int>((cell / d.gx) % d.gy), cell, cell / (static_cast<int64_t>(d.gx) * d.gy)};
+}
+
 // floor(x / div): a multiply-high by magic = ceil(2^32 / div) when the caller
 // set one (exact for its range of x), else a division.
 __device__ __forceinline__ int div_by(int x, int div, uint32_t magic) {
@@ -321,11 +342,9 @@ __global__ void FSCA_FWD_BOUNDS(G) forward_kernel(Dims d, Grid grid, float eps,
        item - (threadIdx.x % 32) / G < items; item += stride) {
     const bool live = item < items;
     const int64_t it = live ? item : items - 1;
-    const int head = static_cast<int>(it % d.heads);
-    const int64_t cell = it / d.heads;
-    const int ix = static_cast<int>(cell % d.gx);
-    const int iy = static_cast<int>((cell / d.gx) % d.gy);
-    const int64_t b = cell / (static_cast<int64_t>(d.gx) * d.gy);
+    const ItemCell ic = item_cell(it, d, items < (int64_t{1} << 31));
+    const int head = ic.head, ix = ic.ix, iy = ic.iy;
+    const int64_t cell = ic.cell, b = ic.b;
     const Cell c{__fadd_rn(grid.xmin, __fmul_rn(static_cast<float>(ix) + 0.5f, grid.sx)),
                  __fadd_rn(grid.ymin, __fmul_rn(static_cast<float>(iy) + 0.5f, grid.sy)), grid.zmin, grid.sz};
     int visible = 0;
@@ -385,11 +404,10 @@ __global__ void FSCA_BWD_BOUNDS(G) backward_kernel(
        item - (threadIdx.x % 32) / G < items; item += stride) {
     const bool live = item < items;
     const int64_t it = live ? item : items - 1;
-    const int head = static_cast<int>(it % d.heads);
-    const int64_t cell = it / d.heads;
-    const int ix = static_cast<int>(cell % d.gx);
-    const int iy = static_cast<int>((cell / d.gx) % d.gy);
-    const int64_t b = cell / (static_cast<int64_t>(d.gx) * d.gy);
+    // 64-bit split in the backward: the 32-bit one measured slower here (1.239 -> 1.249 ms)
+    const ItemCell ic = item_cell(it, d, false);
+    const int head = ic.head, ix = ic.ix, iy = ic.iy;
+    const int64_t cell = ic.cell, b = ic.b;
     const Cell c{__fadd_rn(grid.xmin, __fmul_rn(static_cast<float>(ix) + 0.5f, grid.sx)),
                  __fadd_rn(grid.ymin, __fmul_rn(static_cast<float>(iy) + 0.5f, grid.sy)), grid.zmin, grid.sz};
     int visible = 0;
