@@ -912,9 +912,9 @@ def run_op(args, rank, world, device):
     return line
 
 
-# The reference's only published numbers for this path: the
-# bevformer-1l case, forward-backward scope, p50 of 5 repeats x 100 launches
-# after 20 warm-ups (benchmarks/msda/README.md:72-73 in the muSPACE tree).
+# The reference's only published numbers for this path: the bevformer-1l
+# case, forward-backward scope, p50 of 5 repeats x 100 launches after 20
+# warm-ups (benchmarks/msda/README.md:72-73 in the muSPACE tree).
 PUBLISHED = {
     ("bevformer-1l", torch.float32): {
         "S5000_p50_ms": 4.2387, "S5000_normalised_to_A100_bandwidth_ms": 3.5049, "mmcv_A100_p50_ms": 4.0895,
