@@ -163,3 +163,38 @@ def test_more_landing_pairs_than_a_warp_matches_the_oracle(cuda_device):
     torch.testing.assert_close(out.detach().cpu(), exp[0], rtol=1e-4, atol=1e-4)
     for leaf, ref in zip((leaves[0], leaves[5], leaves[6]), exp[1:]):
         torch.testing.assert_close(leaf.grad.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("grid", [(7, 5, 4), (3, 1, 4)])
+def test_two_batch_entries_with_nonfinite_values_at_32_channels_a_head(cuda_device, grid):
+    """32 channels a head (lane groups of 8, the BEVFormer layout) with two
+    batch entries of 35 (or 3) cells each, and infinite / NaN feature values at
+    pixels of the coarsest level (which every cell samples): the output and
+    every gradient equal the oracle's, the non-finite values receive no
+    gradient, and nothing leaks between batch entries."""
+    t, kw = bevformer_inputs(cuda_device, batch=2, grid=grid, channels=64, heads=2, points=2, seed=7)
+    value = t[0]
+    shapes = t[2].tolist()
+    start3 = int(t[3][3])
+    h3, w3 = shapes[3]
+    value[0, :, start3 : start3 + h3 * w3 : 7, 3] = float("inf")
+    value[1, :, start3 + 3 : start3 + h3 * w3 : 11, 40] = float("nan")
+    value[1, 2, 5, 33] = float("-inf")
+    leaves = list(t)
+    for i in (0, 5, 6):
+        leaves[i] = t[i].clone().requires_grad_(True)
+    out = flash_bevpool_sca(*leaves, **kw)
+    grad = torch.randn(out.shape, generator=torch.Generator().manual_seed(3)).to(cuda_device)
+    out.backward(grad)
+    exp = flash_sca_forward_backward(*[x.cpu() for x in t], kw["grid_size"], kw["voxel_size"], kw["voxel_min"],
+                                     grad.cpu())
+    assert out.abs().sum() > 0 and torch.isfinite(out).all()
+    torch.testing.assert_close(out.detach().cpu(), exp[0], rtol=1e-4, atol=1e-4)
+    for leaf, ref in zip((leaves[0], leaves[5], leaves[6]), exp[1:]):
+        assert torch.isfinite(leaf.grad).all()
+        torch.testing.assert_close(leaf.grad.cpu(), ref, rtol=1e-3, atol=1e-3)
+    # the non-finite values receive no gradient
+    gv = leaves[0].grad
+    assert (gv[0, :, start3 : start3 + h3 * w3 : 7, 3] == 0).all()
+    assert (gv[1, :, start3 + 3 : start3 + h3 * w3 : 11, 40] == 0).all()
