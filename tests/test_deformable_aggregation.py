@@ -252,3 +252,23 @@ def test_point_camera_and_channel_extents_match_the_oracle(cuda_device, pts, cam
     torch.testing.assert_close(got[0].cpu(), expected[0], rtol=1e-4, atol=1e-4)
     for value, ref in zip(got[1:], expected[1:]):
         torch.testing.assert_close(value.cpu(), ref, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.gpu
+def test_a_map_that_leaves_the_features_is_emptied_alike_in_both_kernel_pairs(cuda_device):
+    """A scale whose rows would run past num_feat is emptied on the device by
+    both kernel pairs, so none of its corners is read (its samples have no
+    in-map corner at all): the optimized pair equals the baseline pair."""
+    t, grad = cases.deformable_aggregation_inputs(cuda_device, batch=2, anchors=40, pts=13, cams=3, channels=64,
+                                                  groups=4, active=0.6, seed=3)
+    start = t[2].clone()
+    start[1, 2] = t[0].shape[1] - 5  # the (camera 1, scale 2) map would end past the last feature row
+    t[2] = start
+    opt = _c_abi(t, grad, optimized=True)
+    base = _c_abi(t, grad, optimized=False)
+    torch.cuda.synchronize()
+    assert torch.isfinite(opt[0]).all() and opt[0].abs().sum() > 0
+    torch.testing.assert_close(opt[0], base[0], rtol=1e-4, atol=1e-4)
+    for a, b in zip(opt[1:], base[1:]):
+        torch.testing.assert_close(a, b, rtol=1e-3, atol=1e-3)
+
